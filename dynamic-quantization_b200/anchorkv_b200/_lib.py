@@ -1,0 +1,130 @@
+"""ctypes binding of libanchorkv_b200.so (the C ABI in include/anchorkv_b200.h).
+
+The library is built in-tree (``dynamic-quantization_b200/build.py``) and
+loaded once per process.  There is no fallback: if the library or a CUDA device
+is missing, every compute entry point raises :class:`NativeUnavailableError`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libanchorkv_b200.so"
+
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
+DEV_BAD_DESCRIPTOR, DEV_TIMEOUT = 1, 2
+MODE_SKIP, MODE_INT4, MODE_INT8, MODE_FP16 = 0, 1, 2, 3
+SEM_TENSOR, SEM_PAGE = 0, 1
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+
+_c_p = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+
+# name -> (restype, argtypes); the order follows the header.
+PROTOTYPES = {
+    "akv_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "akv_abi_version": (ctypes.c_int, []),
+    "akv_record_bytes": (_i64, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "akv_quantize": (ctypes.c_int, [_c_p, ctypes.c_int, _i64, _i64, ctypes.c_int, ctypes.c_int,
+                                    _c_p, _c_p, _c_p]),
+    "akv_dequantize": (ctypes.c_int, [_c_p, _c_p, _i64, _i64, ctypes.c_int, _c_p, ctypes.c_int, _c_p]),
+    "akv_pack_pages": (ctypes.c_int, [_c_p, _c_p, _i64, _i64, _i64, _i64, _c_p, _c_p, _i64,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _c_p, _c_p]),
+    "akv_repack_pages": (ctypes.c_int, [_c_p, _c_p, _i64, _c_p, _i64, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_int, _c_p, _c_p]),
+    "akv_unpack_pages": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_int, _c_p, _c_p, _c_p, _c_p]),
+    "akv_workspace_bytes": (_i64, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "akv_decode_partials": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, _c_p, _i32, _c_p, _i64, _i64,
+                                           _i32, _i32, _i32, _i32, _i32, _f32, _i32, _c_p, _c_p, _c_p]),
+    "akv_merge": (ctypes.c_int, [_c_p, _i32, _i32, _i32, _i32, _c_p, _i64, _i64, _c_p, _c_p]),
+    "akv_packed_attention": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, _c_p, _i32, _c_p, _i64, _i64,
+                                            _i32, _i32, _i32, _i32, _i32, _f32, _i32, _c_p, _i64,
+                                            _i64, _c_p, _i64, _c_p, _c_p]),
+}
+
+
+class NativeUnavailableError(RuntimeError):
+    """The CUDA library or a CUDA device is missing; there is no CPU fallback."""
+
+
+class KernelError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load(path: Path | str = LIB_PATH) -> ctypes.CDLL:
+    """Load (once) and return the library with its prototypes set."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            p = Path(path)
+            if not p.exists():
+                raise NativeUnavailableError(
+                    f"{p} is missing; build it with `python dynamic-quantization_b200/build.py`")
+            lib = ctypes.CDLL(str(p))
+            for name, (res, args) in PROTOTYPES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+        return _lib
+
+
+def status_string(status: int) -> str:
+    return load().akv_status_string(status).decode()
+
+
+def call(name: str, *args) -> None:
+    """Call an entry point that returns a status; raise on failure.
+
+    Invalid arguments map to ValueError (the reference's convention for bad
+    geometry), everything else to KernelError."""
+    status = getattr(load(), name)(*args)
+    if status == OK:
+        return
+    msg = f"{name}: {status_string(status)}"
+    if status in (ERR_INVALID, ERR_UNSUPPORTED):
+        raise ValueError(msg)
+    raise KernelError(msg)
+
+
+def require_cuda(tensor, what: str = "tensor") -> None:
+    if not getattr(tensor, "is_cuda", False):
+        raise ValueError(f"{what} must be a CUDA tensor: anchorkv_b200 runs its data plane on the GPU only")
+
+
+def stream_of(device) -> int:
+    import torch
+
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+_status = {}
+
+
+def status_word(device):
+    """The per-device int32 word kernels OR their error bits into."""
+    import torch
+
+    key = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
+    if key not in _status:
+        _status[key] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key))
+    return _status[key]
+
+
+def take_device_status(device=None) -> int:
+    """Synchronise, return and clear the device error bits (0 = no error)."""
+    import torch
+
+    word = status_word(device if device is not None else torch.cuda.current_device())
+    value = int(word.item())
+    word.zero_()
+    return value

@@ -1,0 +1,113 @@
+"""Packed single-token decode attention entry point.
+
+Drop-in for ``src/anchorkv/triton_decode.py:85-104`` (``packed_attention``):
+same arguments, same validation errors, output in the query's dtype and shape.
+It also accepts a :class:`~anchorkv_b200.pool.PagedBatch` (batch of sequences
+over a shared page pool), where the query is ``[batch, Hq, 1, D]``.
+
+The work runs in two sm_100a kernels behind the C ABI (akv_packed_attention):
+the paged split-K decode (one CTA per split x KV head x sequence, bulk-copied
+pages, register dequantisation into mma.sync fragments, fp32 online softmax)
+and the log-sum-exp merge.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .pool import PagedBatch, group_ok
+
+_workspaces: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def _store_geometry(layer):
+    """(arena, arena bytes, table [B, stride], seq_blocks or None, max_blocks)."""
+    if isinstance(layer, PagedBatch):
+        return layer.pool.arena, layer.pool.nbytes, layer.table, layer.seq_blocks, layer.max_blocks
+    n = len(layer.pages)
+    return layer.pool.arena, layer.pool.nbytes, layer.table.view(1, -1), None, n
+
+
+def packed_attention(query, layer, scale, splits=4, *, out=None):
+    """Attend one query token per sequence over the layer's packed pages.
+
+    ``query``: fp16 CUDA ``[batch, Hq, 1, D]`` (batch 1 for a PagedLayer).
+    ``splits``: split-K factor over each sequence's pages (merged by LSE).
+    """
+    batched = isinstance(layer, PagedBatch)
+    batch = layer.batch if batched else 1
+    if query.shape[0] != batch or query.shape[2] != 1 or query.shape[-1] != layer.dim:
+        raise ValueError('packed kernel supports batch=1, query length=1 only' if not batched
+                         else 'query must be [batch, heads, 1, head_dim] for the page table')
+    length = layer.max_blocks if batched else layer.length
+    if query.dtype != torch.float16 or not query.is_cuda or length == 0:
+        raise ValueError('packed kernel requires a nonempty CUDA FP16 cache')
+    if layer.dim not in (64, 128) or layer.block != 16 or not group_ok(layer.dim, layer.group):
+        raise ValueError('supported geometry: block=16, group=32/64/128 or one scale per '
+                         'block and head, head dim=64/128')
+    heads = query.shape[1]
+    if heads % layer.heads:
+        raise ValueError('query heads must be divisible by KV heads')
+    if splits < 1:
+        raise ValueError('splits must be positive')
+    if query.stride(-1) != 1 or query.stride(1) % 8 or query.stride(0) % 8 or query.data_ptr() % 16:
+        query = query.contiguous()
+    arena, arena_bytes, table, seq_blocks, max_blocks = _store_geometry(layer)
+    if out is None:
+        out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+    dev = query.device
+    nbytes = _lib.load().akv_workspace_bytes(batch, heads, splits, layer.dim)
+    ws = _workspace(dev, nbytes)
+    _lib.call("akv_packed_attention", arena.data_ptr(), arena_bytes, table.data_ptr(), table.stride(0),
+              None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks,
+              query.data_ptr(), query.stride(0), query.stride(1), batch, heads, layer.heads, layer.dim,
+              layer.group, float(scale), splits, out.data_ptr(), out.stride(0), out.stride(1),
+              ws.data_ptr(), ws.numel(), _lib.status_word(dev).data_ptr(), _lib.stream_of(dev))
+    return out
+
+
+def decode_partial_states(query, layer, scale, splits=4):
+    """Split-K decode merged to one LSE state per (sequence, query head).
+
+    Returns fp32 ``[batch, Hq, D + 2]`` = (acc[D], m, l) with ``m`` in base-2
+    units of the scaled score, for a further merge (e.g. across GPUs) with
+    :func:`merge_states`."""
+    batched = isinstance(layer, PagedBatch)
+    batch = layer.batch if batched else 1
+    heads = query.shape[1]
+    query = query.contiguous()
+    arena, arena_bytes, table, seq_blocks, max_blocks = _store_geometry(layer)
+    dev = query.device
+    parts = torch.empty((batch, heads, splits, layer.dim + 2), dtype=torch.float32, device=dev)
+    state = torch.empty((batch, heads, layer.dim + 2), dtype=torch.float32, device=dev)
+    stream = _lib.stream_of(dev)
+    _lib.call("akv_decode_partials", arena.data_ptr(), arena_bytes, table.data_ptr(), table.stride(0),
+              None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks, query.data_ptr(),
+              query.stride(0), query.stride(1), batch, heads, layer.heads, layer.dim, layer.group,
+              float(scale), splits, parts.data_ptr(), _lib.status_word(dev).data_ptr(), stream)
+    _lib.call("akv_merge", parts.data_ptr(), batch, heads, splits, layer.dim, None, 0, 0,
+              state.data_ptr(), stream)
+    return state
+
+
+def merge_states(states: torch.Tensor, *, out_dtype=torch.float16) -> torch.Tensor:
+    """Merge ``[n, batch, Hq, D + 2]`` LSE states (e.g. gathered from n GPUs)
+    into the normalised output ``[batch, Hq, 1, D]``."""
+    n, batch, heads, rs = states.shape
+    dim = rs - 2
+    # akv_merge expects [batch][heads][splits][D+2]
+    parts = states.permute(1, 2, 0, 3).contiguous()
+    out = torch.empty((batch, heads, 1, dim), dtype=torch.float16, device=states.device)
+    _lib.call("akv_merge", parts.data_ptr(), batch, heads, n, dim, out.data_ptr(), out.stride(0),
+              out.stride(1), None, _lib.stream_of(states.device))
+    return out if out_dtype == torch.float16 else out.to(out_dtype)

@@ -1,0 +1,477 @@
+// Block codec kernels: symmetric INT8 / packed INT4 with fp16 absmax scales.
+//
+// Bit-exact with the reference quantizers (backend.py:183-226 quantize_tensor,
+// packed_decode.py:48-67 pack_page) because every step is an IEEE operation
+// with the same rounding: fp32 absmax, correctly rounded fp32 division
+// (__fdiv_rn; this file must never be built with fast-math), round half to
+// even (rintf), clamp, and fp16 round-to-nearest-even for the scales.  The
+// page kernels move a 16-token slab per warp with 16-byte vector loads, keep
+// the slab in registers, reduce the group absmax with warp shuffles and write
+// coalesced payload words.
+#include <algorithm>
+
+#include "akv_common.cuh"
+
+namespace akv {
+
+// ============================================================ flat tensors
+// One warp per group of `group` consecutive elements (grid-stride).
+template <typename T, int BITS, int SEM>
+__global__ void __launch_bounds__(256) quantize_flat_kernel(const T *__restrict__ src, int64_t numel,
+                                                            int64_t group, int64_t ngroups,
+                                                            uint8_t *__restrict__ payload,
+                                                            __half *__restrict__ scales) {
+  const float qmax = BITS == 8 ? 127.f : 7.f;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  auto value = [&](int64_t e) -> float {
+    if (e >= numel) return 0.f;  // zero padding of the tail group (backend.py:211-213)
+    float x = to_f32<T>(src[e]);
+    if (SEM == AKV_SEM_PAGE) x = __half2float(__float2half_rn(x));  // pack_page rounds to fp16 first
+    return x;
+  };
+  for (int64_t g = warp; g < ngroups; g += nwarps) {
+    const int64_t base = g * group;
+    float amax = 0.f;
+    for (int64_t i = lane; i < group; i += 32) amax = fmaxf(amax, fabsf(value(base + i)));
+#pragma unroll
+    for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const GroupScale s = group_scale<SEM>(amax, qmax);
+    if (BITS == 8) {
+      int8_t *q = reinterpret_cast<int8_t *>(payload);
+      for (int64_t i = lane; i < group; i += 32)
+        q[base + i] = (int8_t)quantize_value(value(base + i), s.divisor, qmax);
+    } else {
+      for (int64_t i = lane; i < group / 2; i += 32) {
+        const int lo = quantize_value(value(base + 2 * i), s.divisor, qmax);
+        const int hi = quantize_value(value(base + 2 * i + 1), s.divisor, qmax);
+        payload[base / 2 + i] = (uint8_t)((lo & 15) | ((hi & 15) << 4));
+      }
+    }
+    if (lane == 0) scales[g] = s.stored;
+  }
+}
+
+template <typename T, int BITS>
+__global__ void __launch_bounds__(256) dequantize_flat_kernel(const uint8_t *__restrict__ payload,
+                                                              const __half *__restrict__ scales,
+                                                              int64_t numel, int64_t group,
+                                                              T *__restrict__ out) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < numel; i += stride) {
+    int q;
+    if (BITS == 8) {
+      q = (int)reinterpret_cast<const int8_t *>(payload)[i];
+    } else {
+      const int byte = payload[i >> 1];
+      q = (i & 1) ? (byte >> 4) : (byte & 15);
+      q = q >= 8 ? q - 16 : q;  // sign extension (backend.py:172)
+    }
+    out[i] = from_f32<T>((float)q * __half2float(scales[i / group]));
+  }
+}
+
+// ============================================================ page records
+// A slab is one (page, head, K-or-V) 16 x D fp16 tile.  Lane l of the warp owns
+// elements 256*c + 8*l + [0, 8) for chunk c < D/16: one 16-byte fp16 vector per
+// chunk, contiguous across the warp (512 bytes per load instruction).
+template <int D>
+struct Slab {
+  static constexpr int kChunks = D / 16;
+  static constexpr int kElems = kBlock * D;
+};
+
+// Dequantize 8 consecutive elements of a record payload to fp16, exactly as
+// QuantizedPage.dense (packed_decode.py:34-45): fp16(int * float(scale)).
+template <int D, int G>
+__device__ __forceinline__ uint4 record_load8(int mode, const uint8_t *payload, const __half *sc,
+                                              int c, int lane) {
+  const int e = 256 * c + 8 * lane;
+  if (mode == AKV_MODE_FP16) return *reinterpret_cast<const uint4 *>(payload + 2 * e);
+  const float s = __half2float(sc[e / G]);
+  int q[8];
+  if (mode == AKV_MODE_INT8) {
+    const uint2 w = *reinterpret_cast<const uint2 *>(payload + e);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      q[i] = (int)(int8_t)(w.x >> (8 * i));
+      q[4 + i] = (int)(int8_t)(w.y >> (8 * i));
+    }
+  } else {
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(payload + e / 2);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int n = (w >> (4 * i)) & 15;
+      q[i] = n >= 8 ? n - 16 : n;
+    }
+  }
+  uint32_t h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half lo = __float2half_rn((float)q[2 * i] * s);
+    const __half hi = __float2half_rn((float)q[2 * i + 1] * s);
+    h[i] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+  }
+  return make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+// Quantize one slab held in registers (v[c] = 8 fp16 values) into a record.
+template <int D, int G, int SEM>
+__device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], int mode,
+                                           uint8_t *payload, __half *sc, int lane) {
+  constexpr int NC = Slab<D>::kChunks;
+  if (mode == AKV_MODE_FP16) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) *reinterpret_cast<uint4 *>(payload + 512 * c + 16 * lane) = v[c];
+    return;
+  }
+  const float qmax = mode == AKV_MODE_INT8 ? 127.f : 7.f;
+  float x[NC][8];
+  float lm[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+    lm[c] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[c][2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xffff)));
+      x[c][2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
+      lm[c] = fmaxf(lm[c], fmaxf(fabsf(x[c][2 * i]), fabsf(x[c][2 * i + 1])));
+    }
+  }
+  // Group absmax: G/8 lanes share a group inside a chunk (G < 256), or
+  // G/256 whole chunks share one (G >= 256).
+  float gm[NC];
+  if (G < 256) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float m = lm[c];
+#pragma unroll
+      for (int off = 1; off < G / 8; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      gm[c] = m;
+    }
+  } else {
+    constexpr int CPG = G / 256 < NC ? G / 256 : NC;
+#pragma unroll
+    for (int c0 = 0; c0 < NC; c0 += CPG) {
+      float m = 0.f;
+#pragma unroll
+      for (int c = c0; c < c0 + CPG; ++c) m = fmaxf(m, lm[c]);
+#pragma unroll
+      for (int off = 16; off; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+#pragma unroll
+      for (int c = c0; c < c0 + CPG; ++c) gm[c] = m;
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const GroupScale s = group_scale<SEM>(gm[c], qmax);
+    int q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = quantize_value(x[c][i], s.divisor, qmax);
+    const int e = 256 * c + 8 * lane;
+    if (mode == AKV_MODE_INT8) {
+      uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        w0 |= (uint32_t)(q[i] & 0xff) << (8 * i);
+        w1 |= (uint32_t)(q[4 + i] & 0xff) << (8 * i);
+      }
+      *reinterpret_cast<uint2 *>(payload + e) = make_uint2(w0, w1);
+    } else {
+      uint32_t w = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w |= (uint32_t)(q[i] & 15) << (4 * i);
+      *reinterpret_cast<uint32_t *>(payload + e / 2) = w;
+    }
+    if (e % G == 0) sc[e / G] = s.stored;
+  }
+}
+
+// Descriptor check shared by the page kernels.
+__device__ __forceinline__ bool page_in_arena(int64_t desc, int64_t page_bytes, int64_t arena_bytes) {
+  const int64_t off = desc_offset(desc);
+  return (off & 15) == 0 && off >= 0 && off + page_bytes <= arena_bytes;
+}
+
+// Pack (SRC_RECORD = false: dense fp16 source) or repack (SRC_RECORD = true:
+// source records in the arena) one slab per warp.
+template <int D, int G, int SEM, bool SRC_RECORD>
+__global__ void __launch_bounds__(256) pack_pages_kernel(
+    const __half *__restrict__ src_k, const __half *__restrict__ src_v, int64_t outer_stride,
+    int64_t head_stride, int64_t blocks_per_row, const int64_t *__restrict__ src_desc,
+    const int64_t *__restrict__ dst_desc, int64_t n_pages, uint8_t *__restrict__ arena,
+    int64_t arena_bytes, int heads, int32_t *status) {
+  constexpr int NC = Slab<D>::kChunks;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t items = n_pages * heads * 2;
+  for (int64_t it = warp; it < items; it += nwarps) {
+    const int kv = (int)(it & 1);
+    const int h = (int)((it >> 1) % heads);
+    const int64_t p = (it >> 1) / heads;
+    const int64_t dd = dst_desc[p];
+    const int dmode = desc_mode(dd);
+    if (dmode == AKV_MODE_SKIP) continue;
+    const int64_t drec = record_bytes(D, G, dmode);
+    if (!page_in_arena(dd, drec * heads, arena_bytes)) {
+      if (lane == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+      continue;
+    }
+    uint4 v[NC];
+    if (SRC_RECORD) {
+      const int64_t sd = src_desc[p];
+      const int smode = desc_mode(sd);
+      const int64_t srec = record_bytes(D, G, smode);
+      if (smode == AKV_MODE_SKIP || !page_in_arena(sd, srec * heads, arena_bytes)) {
+        if (lane == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+        continue;
+      }
+      const uint8_t *rec = arena + desc_offset(sd) + h * srec;
+      const int64_t pb = payload_bytes(D, smode);
+      const uint8_t *pay = rec + kv * pb;
+      const __half *sc =
+          reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, smode);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) v[c] = record_load8<D, G>(smode, pay, sc, c, lane);
+    } else {
+      const __half *src = (kv ? src_v : src_k) + (p / blocks_per_row) * outer_stride +
+                          h * head_stride + (p % blocks_per_row) * (int64_t)kBlock * D;
+#pragma unroll
+      for (int c = 0; c < NC; ++c)
+        v[c] = __ldg(reinterpret_cast<const uint4 *>(src + 256 * c + 8 * lane));
+    }
+    uint8_t *rec = arena + desc_offset(dd) + h * drec;
+    const int64_t pb = payload_bytes(D, dmode);
+    const int64_t ns = scale_count(D, G, dmode);
+    __half *sc = reinterpret_cast<__half *>(rec + 2 * pb) + kv * ns;
+    store_slab<D, G, SEM>(v, dmode, rec + kv * pb, sc, lane);
+    if (kv == 1) {  // zero the record's alignment pad so records are deterministic
+      const int64_t used = 2 * pb + 4 * ns;
+      if (lane < drec - used) rec[used + lane] = 0;
+    }
+  }
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(256) unpack_pages_kernel(const int64_t *__restrict__ desc,
+                                                           int64_t n_pages,
+                                                           const uint8_t *__restrict__ arena,
+                                                           int64_t arena_bytes, int heads,
+                                                           __half *__restrict__ out_k,
+                                                           __half *__restrict__ out_v,
+                                                           int32_t *status) {
+  constexpr int NC = Slab<D>::kChunks;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t items = n_pages * heads * 2;
+  for (int64_t it = warp; it < items; it += nwarps) {
+    const int kv = (int)(it & 1);
+    const int h = (int)((it >> 1) % heads);
+    const int64_t p = (it >> 1) / heads;
+    __half *out = (kv ? out_v : out_k) + ((int64_t)h * n_pages + p) * kBlock * D;
+    const int64_t d = desc[p];
+    const int mode = desc_mode(d);
+    const int64_t rb = record_bytes(D, G, mode);
+    const bool ok = mode != AKV_MODE_SKIP && page_in_arena(d, rb * heads, arena_bytes);
+    if (mode != AKV_MODE_SKIP && !ok && lane == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (ok) {
+        const uint8_t *rec = arena + desc_offset(d) + h * rb;
+        const int64_t pb = payload_bytes(D, mode);
+        const __half *sc = reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, mode);
+        v = record_load8<D, G>(mode, rec + kv * pb, sc, c, lane);
+      }
+      *reinterpret_cast<uint4 *>(out + 256 * c + 8 * lane) = v;
+    }
+  }
+}
+
+// ================================================================ launchers
+static int grid_for(int64_t warps_needed) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t blocks = (warps_needed + 7) / 8;  // 8 warps per 256-thread block
+  return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)sms * 16));
+}
+
+static int launch_status() {
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+}
+
+// G values the page kernels are instantiated for: 32, 64, 128 (per-row groups)
+// and 16*D (one scale per 16-token slab, i.e. per block and KV head).
+template <int D, template <int, int> class F, typename... Args>
+static int dispatch_group(int group, Args... args) {
+  switch (group) {
+    case 32: return F<D, 32>::run(args...);
+    case 64: return F<D, 64>::run(args...);
+    case 128: return F<D, 128>::run(args...);
+    case 16 * D: return F<D, 16 * D>::run(args...);
+    default: return AKV_ERR_UNSUPPORTED;
+  }
+}
+
+struct PackArgs {
+  const void *src_k, *src_v;
+  int64_t outer_stride, head_stride, blocks_per_row;
+  const int64_t *src_desc, *dst_desc;
+  int64_t n_pages;
+  void *arena;
+  int64_t arena_bytes;
+  int heads, semantics;
+  int32_t *status;
+  cudaStream_t stream;
+};
+
+template <int D, int G>
+struct PackLaunch {
+  static int run(const PackArgs &a, bool repack) {
+    const int grid = grid_for(a.n_pages * a.heads * 2);
+#define AKV_PACK(SEM, REC)                                                                      \
+  pack_pages_kernel<D, G, SEM, REC><<<grid, 256, 0, a.stream>>>(                                \
+      (const __half *)a.src_k, (const __half *)a.src_v, a.outer_stride, a.head_stride,          \
+      a.blocks_per_row, a.src_desc, a.dst_desc, a.n_pages, (uint8_t *)a.arena, a.arena_bytes, \
+      a.heads, a.status)
+    if (repack) {
+      if (a.semantics == AKV_SEM_PAGE) AKV_PACK(AKV_SEM_PAGE, true);
+      else AKV_PACK(AKV_SEM_TENSOR, true);
+    } else {
+      if (a.semantics == AKV_SEM_PAGE) AKV_PACK(AKV_SEM_PAGE, false);
+      else AKV_PACK(AKV_SEM_TENSOR, false);
+    }
+#undef AKV_PACK
+    return launch_status();
+  }
+};
+
+struct UnpackArgs {
+  const int64_t *desc;
+  int64_t n_pages;
+  const void *arena;
+  int64_t arena_bytes;
+  int heads;
+  void *out_k, *out_v;
+  int32_t *status;
+  cudaStream_t stream;
+};
+
+template <int D, int G>
+struct UnpackLaunch {
+  static int run(const UnpackArgs &a) {
+    unpack_pages_kernel<D, G><<<grid_for(a.n_pages * a.heads * 2), 256, 0, a.stream>>>(
+        a.desc, a.n_pages, (const uint8_t *)a.arena, a.arena_bytes, a.heads, (__half *)a.out_k,
+        (__half *)a.out_v, a.status);
+    return launch_status();
+  }
+};
+
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace akv
+
+using namespace akv;
+
+extern "C" int akv_quantize(const void *src, int src_dtype, int64_t numel, int64_t group, int bits,
+                            int semantics, void *payload, void *scales, void *stream) {
+  if (!src || !payload || !scales || numel <= 0 || group <= 0) return AKV_ERR_INVALID;
+  if (bits != 4 && bits != 8) return AKV_ERR_INVALID;
+  if (bits == 4 && group % 2) return AKV_ERR_INVALID;
+  if (semantics != AKV_SEM_TENSOR && semantics != AKV_SEM_PAGE) return AKV_ERR_INVALID;
+  const int64_t ngroups = (numel + group - 1) / group;
+  const int grid = grid_for(ngroups);
+  cudaStream_t s = (cudaStream_t)stream;
+#define AKV_Q(T, B, S)                                                                   \
+  quantize_flat_kernel<T, B, S><<<grid, 256, 0, s>>>((const T *)src, numel, group, ngroups, \
+                                                       (uint8_t *)payload, (__half *)scales)
+#define AKV_QB(T, S) \
+  if (bits == 8) AKV_Q(T, 8, S); else AKV_Q(T, 4, S)
+#define AKV_QS(T) \
+  if (semantics == AKV_SEM_TENSOR) { AKV_QB(T, AKV_SEM_TENSOR); } else { AKV_QB(T, AKV_SEM_PAGE); }
+  switch (src_dtype) {
+    case AKV_DTYPE_F32: AKV_QS(float); break;
+    case AKV_DTYPE_F16: AKV_QS(__half); break;
+    case AKV_DTYPE_BF16: AKV_QS(__nv_bfloat16); break;
+    default: return AKV_ERR_INVALID;
+  }
+#undef AKV_QS
+#undef AKV_QB
+#undef AKV_Q
+  return launch_status();
+}
+
+extern "C" int akv_dequantize(const void *payload, const void *scales, int64_t numel, int64_t group,
+                              int bits, void *out, int out_dtype, void *stream) {
+  if (!payload || !scales || !out || numel <= 0 || group <= 0) return AKV_ERR_INVALID;
+  if (bits != 4 && bits != 8) return AKV_ERR_INVALID;
+  const int grid = grid_for((numel + 31) / 32);
+  cudaStream_t s = (cudaStream_t)stream;
+#define AKV_D(T)                                                                           \
+  if (bits == 8)                                                                           \
+    dequantize_flat_kernel<T, 8><<<grid, 256, 0, s>>>((const uint8_t *)payload,            \
+                                                       (const __half *)scales, numel, group, (T *)out); \
+  else                                                                                     \
+    dequantize_flat_kernel<T, 4><<<grid, 256, 0, s>>>((const uint8_t *)payload,            \
+                                                       (const __half *)scales, numel, group, (T *)out)
+  switch (out_dtype) {
+    case AKV_DTYPE_F32: AKV_D(float); break;
+    case AKV_DTYPE_F16: AKV_D(__half); break;
+    case AKV_DTYPE_BF16: AKV_D(__nv_bfloat16); break;
+    default: return AKV_ERR_INVALID;
+  }
+#undef AKV_D
+  return launch_status();
+}
+
+static int check_page_geometry(int heads, int head_dim, int group) {
+  if (heads <= 0) return AKV_ERR_INVALID;
+  if (head_dim != 64 && head_dim != 128) return AKV_ERR_UNSUPPORTED;
+  if (group != 32 && group != 64 && group != 128 && group != 16 * head_dim) return AKV_ERR_UNSUPPORTED;
+  return AKV_OK;
+}
+
+extern "C" int akv_pack_pages(const void *src_k, const void *src_v, int64_t outer_stride,
+                              int64_t head_stride, int64_t blocks_per_row, int64_t n_pages,
+                              const int64_t *dst_desc, void *arena, int64_t arena_bytes, int heads,
+                              int head_dim, int group, int semantics, int32_t *dev_status,
+                              void *stream) {
+  if (int st = check_page_geometry(heads, head_dim, group)) return st;
+  if (!src_k || !src_v || !dst_desc || !arena || n_pages < 0 || blocks_per_row <= 0) return AKV_ERR_INVALID;
+  if (!aligned16(src_k) || !aligned16(src_v) || !aligned16(arena)) return AKV_ERR_INVALID;
+  if ((outer_stride * 2) % 16 || (head_stride * 2) % 16) return AKV_ERR_INVALID;
+  if (semantics != AKV_SEM_TENSOR && semantics != AKV_SEM_PAGE) return AKV_ERR_INVALID;
+  if (n_pages == 0) return AKV_OK;
+  PackArgs a{src_k, src_v, outer_stride, head_stride, blocks_per_row, nullptr, dst_desc, n_pages,
+             arena, arena_bytes, heads, semantics, dev_status, (cudaStream_t)stream};
+  return head_dim == 64 ? dispatch_group<64, PackLaunch>(group, a, false)
+                        : dispatch_group<128, PackLaunch>(group, a, false);
+}
+
+extern "C" int akv_repack_pages(const int64_t *src_desc, const int64_t *dst_desc, int64_t n_pages,
+                                void *arena, int64_t arena_bytes, int heads, int head_dim, int group,
+                                int32_t *dev_status, void *stream) {
+  if (int st = check_page_geometry(heads, head_dim, group)) return st;
+  if (!src_desc || !dst_desc || !arena || n_pages < 0 || !aligned16(arena)) return AKV_ERR_INVALID;
+  if (n_pages == 0) return AKV_OK;
+  PackArgs a{nullptr, nullptr, 0, 0, 1, src_desc, dst_desc, n_pages, arena, arena_bytes, heads,
+             AKV_SEM_PAGE, dev_status, (cudaStream_t)stream};
+  return head_dim == 64 ? dispatch_group<64, PackLaunch>(group, a, true)
+                        : dispatch_group<128, PackLaunch>(group, a, true);
+}
+
+extern "C" int akv_unpack_pages(const int64_t *desc, int64_t n_pages, const void *arena,
+                                int64_t arena_bytes, int heads, int head_dim, int group, void *out_k,
+                                void *out_v, int32_t *dev_status, void *stream) {
+  if (int st = check_page_geometry(heads, head_dim, group)) return st;
+  if (!desc || !arena || !out_k || !out_v || n_pages < 0) return AKV_ERR_INVALID;
+  if (!aligned16(arena) || !aligned16(out_k) || !aligned16(out_v)) return AKV_ERR_INVALID;
+  if (n_pages == 0) return AKV_OK;
+  UnpackArgs a{desc, n_pages, arena, arena_bytes, heads, out_k, out_v, dev_status, (cudaStream_t)stream};
+  return head_dim == 64 ? dispatch_group<64, UnpackLaunch>(group, a)
+                        : dispatch_group<128, UnpackLaunch>(group, a);
+}

@@ -1,0 +1,157 @@
+/*
+ * anchorkv_b200 -- C ABI of the B200 (sm_100a) packed-KV decode path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*, a cudaStream_t; NULL means the legacy default stream),
+ * returns an int status (AKV_OK on success), launches asynchronously on that
+ * stream and allocates nothing: the caller owns every buffer, including the
+ * split-K workspace.  The library keeps no mutable global state, so concurrent
+ * calls on different streams are independent.
+ *
+ * Reference interfaces each entry point replaces are cited by file:line in
+ * the reference project (Dev-Sinha13/Dynamic-Quantization, src/anchorkv/).
+ *
+ * Physical page format (the layout kernels read and write):
+ *   - a page is `block` = 16 tokens of K and V for all KV heads of one
+ *     (sequence, layer); it lives at a 16-byte aligned byte offset in an arena;
+ *   - the page holds `heads` head records back to back, each
+ *     akv_record_bytes(head_dim, group, mode) bytes:
+ *       [K payload][V payload][K scales][V scales][zero pad to 16 bytes]
+ *     payload = 16 rows x head_dim, row-major, fp16 / int8 / two's-complement
+ *     nibbles with the even element in the low nibble (the reference byte
+ *     layout); scales = fp16, element (row, col) uses scale (row*head_dim+col)/group;
+ *   - a page descriptor is an int64:
+ *       bits 0-1  mode (AKV_MODE_*; AKV_MODE_SKIP = evicted or not visible)
+ *       bits 2-5  valid tokens in the page minus one (0..15)
+ *       bits 8-63 byte offset of the page in the arena (16-byte aligned).
+ */
+#ifndef ANCHORKV_B200_H
+#define ANCHORKV_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Host status codes. */
+#define AKV_OK 0
+#define AKV_ERR_INVALID 1     /* bad argument: null pointer, size, alignment, dtype */
+#define AKV_ERR_UNSUPPORTED 2 /* well-formed but unsupported geometry */
+#define AKV_ERR_CUDA 3        /* CUDA error when launching */
+
+/* Bits a kernel ORs into the optional device status word (int32, caller owned). */
+#define AKV_DEV_BAD_DESCRIPTOR 1 /* descriptor outside the arena or misaligned; page skipped */
+#define AKV_DEV_TIMEOUT 2        /* a bounded wait on a bulk copy gave up */
+
+/* Page modes (descriptor bits 0-1). */
+#define AKV_MODE_SKIP 0
+#define AKV_MODE_INT4 1
+#define AKV_MODE_INT8 2
+#define AKV_MODE_FP16 3
+
+/* Quantizer semantics: the reference has two, and they are not bitwise equal. */
+#define AKV_SEM_TENSOR 0 /* backend.quantize_tensor: fp32 scale divisor, scale 1 for zero groups */
+#define AKV_SEM_PAGE 1   /* packed_decode.pack_page: fp16 scale divisor, scale >= 2^-14 */
+
+/* Element types. */
+#define AKV_DTYPE_F32 0
+#define AKV_DTYPE_F16 1
+#define AKV_DTYPE_BF16 2
+
+/* Message for a host status code. */
+const char *akv_status_string(int status);
+
+/* ABI version, bumped on any incompatible change. */
+int akv_abi_version(void);
+
+/* Bytes of one (page, head) record for a mode (0 for AKV_MODE_SKIP); -1 for an
+ * unsupported geometry.  Replaces the byte accounting of QuantizedPage.nbytes
+ * (packed_decode.py:28-32), rounded up to 16 bytes. */
+int64_t akv_record_bytes(int head_dim, int group, int mode);
+
+/* Quantize a flat tensor of `numel` elements in groups of `group` (zero padded
+ * to a whole group) to symmetric INT8 or packed INT4.
+ * payload: int8[padded] (bits 8) or uint8[padded/2] (bits 4); scales: fp16[padded/group].
+ * Replaces backend.quantize_tensor (backend.py:183-226) with AKV_SEM_TENSOR and
+ * the data plane of packed_decode.pack_page (packed_decode.py:48-67) with AKV_SEM_PAGE. */
+int akv_quantize(const void *src, int src_dtype, int64_t numel, int64_t group, int bits,
+                 int semantics, void *payload, void *scales, void *stream);
+
+/* Dequantize `numel` elements: out = dtype(int * float(scale)).
+ * Replaces PackedTensor.dequantize (backend.py:154-180) and QuantizedPage.dense
+ * (packed_decode.py:34-45). */
+int akv_dequantize(const void *payload, const void *scales, int64_t numel, int64_t group,
+                   int bits, void *out, int out_dtype, void *stream);
+
+/* Quantize/pack dense fp16 K and V into page records.  Page p covers source
+ * rows (p / blocks_per_row, tokens (p % blocks_per_row)*16 .. +15) of
+ * src[outer][head][token][head_dim] (strides in elements, head_dim contiguous);
+ * dst_desc[p] gives its mode and offset.  Bit-exact with quantize_tensor
+ * (AKV_SEM_TENSOR, group dividing 16*head_dim) or pack_page (AKV_SEM_PAGE).
+ * Replaces the per-block quantize_tensor loop of requantize_segment
+ * (backend.py:470-483) and PagedLayer's page packing (packed_decode.py:144-174). */
+int akv_pack_pages(const void *src_k, const void *src_v, int64_t outer_stride,
+                   int64_t head_stride, int64_t blocks_per_row, int64_t n_pages,
+                   const int64_t *dst_desc, void *arena, int64_t arena_bytes, int heads,
+                   int head_dim, int group, int semantics, int32_t *dev_status, void *stream);
+
+/* Requantize pages in the arena: dequantize src records to fp16 exactly as
+ * QuantizedPage.dense does, then pack with pack_page semantics into dst records.
+ * Replaces PagedLayer.demote (packed_decode.py:164-174). Source and
+ * destination records must not overlap. */
+int akv_repack_pages(const int64_t *src_desc, const int64_t *dst_desc, int64_t n_pages,
+                     void *arena, int64_t arena_bytes, int heads, int head_dim, int group,
+                     int32_t *dev_status, void *stream);
+
+/* Dequantize pages to dense fp16 out_k/out_v[heads][n_pages*16][head_dim]
+ * (skipped pages read as zeros).  Replaces PagedLayer.dense (packed_decode.py:189-194). */
+int akv_unpack_pages(const int64_t *desc, int64_t n_pages, const void *arena,
+                     int64_t arena_bytes, int heads, int head_dim, int group, void *out_k,
+                     void *out_v, int32_t *dev_status, void *stream);
+
+/* Workspace bytes akv_packed_attention needs. */
+int64_t akv_workspace_bytes(int batch, int q_heads, int splits, int head_dim);
+
+/* Split-K paged decode attention: one query token per sequence over mixed
+ * FP16/INT8/INT4 pages.
+ *   table: descriptors, sequence b's pages at table[b*table_stride + j], j < blocks(b);
+ *   seq_blocks: per-sequence page count (NULL: every sequence has max_blocks);
+ *   query: fp16 [batch][q_heads][head_dim] with the given strides (elements);
+ *   q head h attends KV head h / (q_heads / kv_heads);
+ *   partials: fp32 [batch][q_heads][splits][head_dim + 2] = (acc[head_dim], m, l),
+ *   m in base-2 units of the scaled score, acc and l relative to 2^m.
+ * Replaces triton_decode._decode_parts (triton_decode.py:35-67). */
+int akv_decode_partials(const void *arena, int64_t arena_bytes, const int64_t *table,
+                        int64_t table_stride, const int32_t *seq_blocks, int32_t max_blocks,
+                        const void *query, int64_t q_batch_stride, int64_t q_head_stride,
+                        int32_t batch, int32_t q_heads, int32_t kv_heads, int32_t head_dim,
+                        int32_t group, float scale, int32_t splits, float *partials,
+                        int32_t *dev_status, void *stream);
+
+/* Log-sum-exp merge of `splits` partial states per (sequence, query head).
+ * out (nullable): fp16 [batch][q_heads][head_dim] with strides (elements);
+ * state_out (nullable): fp32 [batch][q_heads][head_dim + 2] merged (acc, m, l)
+ * for a further merge (e.g. across GPUs).  Empty splits weigh 0; a query with
+ * no visible token gets zeros.
+ * Replaces triton_decode._merge_parts (triton_decode.py:70-82). */
+int akv_merge(const float *partials, int32_t batch, int32_t q_heads, int32_t splits,
+              int32_t head_dim, void *out, int64_t out_batch_stride, int64_t out_head_stride,
+              float *state_out, void *stream);
+
+/* akv_decode_partials followed by akv_merge, partials in the caller's workspace
+ * (at least akv_workspace_bytes bytes).
+ * Replaces triton_decode.packed_attention (triton_decode.py:85-104). */
+int akv_packed_attention(const void *arena, int64_t arena_bytes, const int64_t *table,
+                         int64_t table_stride, const int32_t *seq_blocks, int32_t max_blocks,
+                         const void *query, int64_t q_batch_stride, int64_t q_head_stride,
+                         int32_t batch, int32_t q_heads, int32_t kv_heads, int32_t head_dim,
+                         int32_t group, float scale, int32_t splits, void *out,
+                         int64_t out_batch_stride, int64_t out_head_stride, void *workspace,
+                         int64_t workspace_bytes, int32_t *dev_status, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANCHORKV_B200_H */

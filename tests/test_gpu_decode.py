@@ -1,0 +1,159 @@
+"""Packed decode attention on the GPU against the reference fixtures and the oracle.
+
+Tolerance: max-abs 2e-3 and relative 1e-2 against the float64 oracle and the
+reference's fp16 SDPA output (fp16 inputs, fp32 accumulation)."""
+
+import json
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import anchorkv_b200 as akv
+import workloads as W
+from anchorkv_b200 import pool as P
+from paged_reference import paged_decode_f64
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+GOLDEN = Path(__file__).resolve().parent / "golden"
+ATTN = np.load(GOLDEN / "attention.npz")
+META = json.loads((GOLDEN / "attention.json").read_text())
+BITS = {"fp16": 16, "int8": 8, "int4": 4, "evicted": 0}
+
+
+def _close(actual: torch.Tensor, expected, atol=ATOL, rtol=RTOL):
+    a = actual.detach().float().cpu().numpy().reshape(-1)
+    e = np.asarray(expected, np.float64).reshape(-1)
+    np.testing.assert_allclose(a, e, atol=atol, rtol=rtol)
+
+
+@pytest.mark.parametrize("meta", META["gate"], ids=lambda m: m["key"])
+def test_kernel_gate_against_reference(cuda, meta):
+    """The reference's GPU acceptance gate (colab_experiment.py:271-291) on the
+    same inputs: page lifecycle, dense values and packed output."""
+    q, k, v = (t.to(cuda) for t in W.gate_workload(meta["dim"], meta["length"], meta["seed"]))
+    layer = akv.PagedLayer(2, meta["dim"], 128, archive_bits=meta["bits"], protected=(0,),
+                           recent_pages=1, device=cuda)
+    for begin in range(0, meta["length"], 7):
+        layer.append(k[:, :, begin:begin + 7], v[:, :, begin:begin + 7])
+    assert [pair[0].bits for pair in layer.pages] == meta["page_bits"]
+    assert layer.demotions == meta["demotions"]
+    assert layer.payload_bytes == meta["payload_bytes"]
+    dk, dv = layer.dense()
+    assert W.sha256(dk, dv) == meta["dense_sha"]
+    out = akv.packed_attention(q, layer, meta["dim"] ** -0.5)
+    assert out.shape == q.shape and out.dtype == torch.float16
+    golden = ATTN[meta["key"]]
+    _close(out, golden.astype(np.float64))
+    ref = akv.dense_attention(q, layer, meta["dim"] ** -0.5)
+    _close(out, ref.float().cpu().numpy())
+    assert akv.take_device_status(cuda) == 0
+
+
+@pytest.mark.parametrize("meta", META["parity"], ids=lambda m: m["key"])
+@pytest.mark.parametrize("splits", [1, 4, 7])
+def test_parity_workload_against_reference(cuda, meta, splits):
+    """16 query / 8 KV heads, 512 tokens, per-block-per-head scales, FP16/INT8/INT4
+    blocks, evicted blocks and focus/local visibility (backend.py:530-591)."""
+    q, k, v, _ = W.parity_workload(meta["seed"])
+    bits = np.array([BITS[m] for m in meta["modes"]])[None]
+    visible = np.array([[i in set(meta["visible"]) for i in range(bits.shape[1])]])
+    counts = {b: int((bits == b).sum()) for b in (16, 8, 4)}
+    pool = P.PagePool(8, 128, group=2048, pages=counts, device=cuda, shuffle_seed=1)
+    store = P.pack_dense(pool, k.to(cuda), v.to(cuda), bits, visible=visible, semantics="tensor")
+    out = akv.packed_attention(q.to(cuda), store, 1 / math.sqrt(128), splits=splits)
+    _close(out, ATTN[meta["key"]].astype(np.float64))
+    oracle = paged_decode_f64(q[:, :, 0].numpy(), k.numpy(), v.numpy(), bits, 1 / math.sqrt(128),
+                              group=2048, visible=visible)
+    _close(out, oracle)
+    assert akv.take_device_status(cuda) == 0
+
+
+CASES = [
+    # dim, q_heads, kv_heads, group, semantics, splits, lengths
+    (128, 16, 8, 2048, "tensor", 4, [512, 333, 17]),
+    (128, 32, 8, 2048, "tensor", 8, [200, 16, 1]),
+    (128, 8, 8, 64, "page", 3, [97, 65]),
+    (128, 64, 8, 64, "page", 2, [129]),
+    (128, 4, 1, 128, "page", 64, [300]),
+    (64, 4, 2, 64, "page", 4, [97, 33, 15]),
+    (64, 8, 1, 1024, "tensor", 5, [250, 64]),
+    (64, 16, 16, 32, "page", 1, [40]),
+    (128, 32, 2, 2048, "tensor", 3, [100, 50]),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"d{c[0]}_q{c[1]}_kv{c[2]}_g{c[3]}_s{c[5]}")
+def test_random_batches_against_oracle(cuda, case):
+    dim, hq, hkv, group, semantics, splits, lengths = case
+    batch, tokens = len(lengths), max(lengths)
+    nblk = -(-tokens // 16)
+    seed = dim + hq * 3 + group + splits
+    k = W.outlier_kv(seed, (batch, hkv, tokens, dim))
+    v = W.outlier_kv(seed + 1, (batch, hkv, tokens, dim))
+    q = W.normal(seed + 2, (batch, hq, 1, dim))
+    bits = np.array(W.draw_modes(seed + 3, batch * nblk, {16: .2, 8: .3, 4: .4, 0: .1})).reshape(batch, nblk)
+    visible = np.array(W.draw_modes(seed + 4, batch * nblk, {16: .9, 0: .1})).reshape(batch, nblk) > 0
+    counts = {b: int((bits == b).sum()) for b in (16, 8, 4)}
+    pool = P.PagePool(hkv, dim, group=group, pages=counts, device=cuda, shuffle_seed=seed)
+    store = P.pack_dense(pool, k.to(cuda), v.to(cuda), bits, visible=visible, semantics=semantics,
+                         lengths=lengths)
+    scale = 1 / math.sqrt(dim)
+    out = akv.packed_attention(q.to(cuda), store, scale, splits=splits)
+    oracle = paged_decode_f64(q[:, :, 0].numpy(), k.numpy(), v.numpy(), bits, scale, group=group,
+                              semantics=semantics, visible=visible, lengths=lengths)
+    _close(out, oracle)
+    assert akv.take_device_status(cuda) == 0
+
+
+def test_fully_masked_sequence_outputs_zeros(cuda):
+    k = W.outlier_kv(1, (2, 2, 64, 128))
+    q = W.normal(2, (2, 4, 1, 128)).to(cuda)
+    bits = np.array([[16, 8, 4, 4], [0, 0, 0, 0]])
+    pool = P.PagePool(2, 128, group=64, pages={16: 1, 8: 1, 4: 2}, device=cuda)
+    store = P.pack_dense(pool, k.to(cuda), k.to(cuda), bits, semantics="page")
+    out = akv.packed_attention(q, store, 0.1, splits=3)
+    assert torch.isfinite(out).all()
+    assert (out[1] == 0).all()
+
+
+def test_sharded_states_merge_to_full_result(cuda):
+    """Contiguous sequence shards merged by LSE state equal the unsharded decode
+    (the long-context multi-GPU algebra, emulated on one GPU)."""
+    tokens, dim = 16 * 40, 128
+    k = W.outlier_kv(21, (1, 8, tokens, dim))
+    v = W.outlier_kv(22, (1, 8, tokens, dim))
+    q = W.normal(23, (1, 32, 1, dim)).to(cuda)
+    bits = np.array(W.draw_modes(24, 40, {16: .05, 8: .25, 4: .7}))[None]
+    counts = {b: int((bits == b).sum()) for b in (16, 8, 4)}
+    pool = P.PagePool(8, dim, group=2048, pages=counts, device=cuda)
+    full = P.pack_dense(pool, k.to(cuda), v.to(cuda), bits)
+    ref = akv.packed_attention(q, full, 0.088, splits=5)
+    states = []
+    for lo, hi in ((0, 13), (13, 27), (27, 40)):
+        shard = P.PagedBatch(pool, 1, hi - lo)
+        shard.table.copy_(full.table[:, lo:hi])
+        states.append(akv.decode_partial_states(q, shard, 0.088, splits=3))
+    out = akv.merge_states(torch.stack(states))
+    _close(out, ref.float().cpu().numpy(), atol=1e-3, rtol=1e-3)
+
+
+def test_out_of_arena_descriptor_is_skipped_and_reported(cuda):
+    k = W.outlier_kv(31, (1, 2, 48, 64))
+    q = W.normal(32, (1, 2, 1, 64)).to(cuda)
+    pool = P.PagePool(2, 64, group=64, pages={16: 3}, device=cuda)
+    store = P.pack_dense(pool, k.to(cuda), k.to(cuda), [[16, 16, 16]], semantics="page")
+    good = akv.packed_attention(q, store, 0.125)
+    ref_two = P.PagedBatch(pool, 1, 2)
+    ref_two.table.copy_(store.table[:, :2])
+    expect = akv.packed_attention(q, ref_two, 0.125)
+    assert akv.take_device_status(cuda) == 0
+    store.table[0, 2] = P.encode(16, 16, pool.nbytes + 4096)  # beyond the arena: bounds check skips it
+    bad = akv.packed_attention(q, store, 0.125)
+    assert akv.take_device_status(cuda) & 1
+    torch.testing.assert_close(bad, expect)
+    assert not torch.equal(good, expect)

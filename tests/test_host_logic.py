@@ -1,0 +1,138 @@
+"""Host-side logic that needs no GPU: descriptors, pool bookkeeping, the
+declarative parser and the block-store lifecycle (data plane replaced by the
+oracle in this test only)."""
+
+import numpy as np
+import pytest
+import torch
+
+import anchorkv_b200 as akv
+from anchorkv_b200 import backend as B
+from anchorkv_b200 import pool as P
+from anchorkv_b200.policy import CacheMode
+from oracle import codec as OC
+
+_KERNEL_QUANTIZE = B.quantize_tensor  # FP16/EVICTED modes need no kernel
+
+
+def test_descriptor_round_trip():
+    for bits in (4, 8, 16):
+        for ntok in (1, 7, 16):
+            for off in (0, 16, 4096 * 123, (1 << 40) + 48):
+                assert P.decode(P.encode(bits, ntok, off)) == (bits, ntok, off)
+    assert P.encode(None, 5, 0) == 0 and P.decode(0)[0] is None
+    with pytest.raises(ValueError):
+        P.encode(4, 0, 0)
+    with pytest.raises(ValueError):
+        P.encode(4, 3, 8)
+    codes = np.array([1, 2, 3, 0])
+    arr = P.encode_array(codes, np.array([16, 3, 1, 9]), np.array([32, 64, 0, 16]))
+    assert list(arr) == [P.encode(4, 16, 32), P.encode(8, 3, 64), P.encode(16, 1, 0), 0]
+
+
+def test_record_sizes_are_reference_bytes_plus_pad():
+    # QuantizedPage.nbytes per head: payload + scales (packed_decode.py:28-32)
+    assert P.algorithmic_record_bytes(128, 2048, 4) == 2 * 1024 + 4
+    assert P.record_bytes(128, 2048, 4) == 2064
+    assert P.algorithmic_record_bytes(128, 64, 8) == P.record_bytes(128, 64, 8) == 4096 + 128
+    assert P.record_bytes(128, 64, 16) == 8192
+
+
+def test_parser_matches_reference_behaviour():
+    parser = akv.DeclarativeAttentionParser()
+    assert parser.feed("reason <fo") == ()
+    focus = parser.feed('cus magic_chunks="2, 3">inspect')
+    closing = parser.feed("</focus><local>")
+    anchor = parser.feed("<anchor segments='4, 4'>")
+    assert focus[0].mode == akv.AttentionMode.FOCUS and focus[0].segment_ids == (2, 3)
+    assert closing[0].mode == akv.AttentionMode.GLOBAL and closing[1].mode == akv.AttentionMode.LOCAL
+    assert anchor[0].kind == akv.DirectiveKind.ANCHOR and anchor[0].segment_ids == (4,)
+    assert parser.state.mode == akv.AttentionMode.LOCAL
+    with pytest.raises(ValueError, match="missing a segment list"):
+        akv.DeclarativeAttentionParser().feed("<focus>")
+    p2 = akv.DeclarativeAttentionParser()
+    with pytest.raises(ValueError):
+        p2.feed("<archive>")
+    assert p2.feed("<global>")[0].mode == akv.AttentionMode.GLOBAL  # bad tag was consumed
+
+
+def _oracle_quantize(tensor, mode, *, group_size=64):
+    """CPU stand-in for the kernel, used only to exercise host logic here."""
+    mode = CacheMode(getattr(mode, "value", mode))
+    if mode in (CacheMode.FP16, CacheMode.EVICTED):
+        return _KERNEL_QUANTIZE(tensor, mode, group_size=group_size)
+    bits = 8 if mode is CacheMode.INT8 else 4
+    payload, scales = OC.quantize_tensor(tensor.detach().float().numpy(), bits, group_size)
+    return B.PackedTensor(mode, tuple(tensor.shape), tensor.dtype, torch.from_numpy(payload),
+                          torch.from_numpy(scales), group_size, tensor.numel())
+
+
+def _oracle_dequantize(self, *, dtype=None, device=None):
+    if self.mode is CacheMode.EVICTED or self.payload is None:
+        raise RuntimeError("evicted tensors cannot be materialized")
+    out_dtype = self.original_dtype if dtype is None else dtype
+    if self.mode is CacheMode.FP16:
+        return self.payload.to(out_dtype).reshape(self.shape)
+    bits = 8 if self.mode is CacheMode.INT8 else 4
+    vals = OC.dequantize_tensor(self.payload.numpy(), self.scales.numpy(), bits, self.group_size,
+                                self.original_numel)
+    return torch.from_numpy(vals).reshape(self.shape).to(out_dtype)
+
+
+@pytest.fixture
+def cpu_cache(monkeypatch):
+    monkeypatch.setattr(B, "quantize_tensor", _oracle_quantize)
+    monkeypatch.setattr(B.PackedTensor, "dequantize", _oracle_dequantize)
+    torch.manual_seed(11)
+    cache = akv.DeclarativeKVCache(block_size=4, group_size=16)
+    for sid, start, count, role in [(0, 0, 4, akv.SegmentRole.SINK), (1, 4, 6, akv.SegmentRole.CONTEXT),
+                                    (2, 10, 6, akv.SegmentRole.CONTEXT), (3, 16, 4, akv.SegmentRole.RESPONSE)]:
+        cache.add_segment(sid, torch.randn(1, 2, count, 8), torch.randn(1, 2, count, 8),
+                          token_start=start, role=role)
+    return cache
+
+
+def test_block_store_lifecycle_rules(cpu_cache):
+    c = cpu_cache
+    assert [len(c._segment_blocks[s]) for s in range(4)] == [1, 2, 2, 1]
+    with pytest.raises(ValueError, match="overlap"):
+        c.add_segment(9, torch.randn(1, 2, 3, 8), torch.randn(1, 2, 3, 8), token_start=2)
+    with pytest.raises(ValueError, match="already registered"):
+        c.add_segment(0, torch.randn(1, 2, 3, 8), torch.randn(1, 2, 3, 8), token_start=40)
+    before = c.resident_bytes
+    c.requantize_segment(1, CacheMode.INT8)
+    c.requantize_segment(1, CacheMode.INT4)
+    assert c.resident_bytes < before
+    with pytest.raises(akv.LossyPromotionError):
+        c.requantize_segment(1, CacheMode.INT8)
+    c.protect_segment(2)
+    with pytest.raises(ValueError, match="protected"):
+        c.requantize_segment(2, CacheMode.INT4)
+    c.requantize_segment(1, CacheMode.EVICTED)
+    assert c.visible_segment_ids() == (0, 2, 3)
+    with pytest.raises(RuntimeError, match="no resident"):
+        c.materialize_segments([1])
+    c.feed_declarations('<focus segments="2">')
+    mat = c.materialize_visible(dtype=torch.float32)
+    assert mat.positions.tolist() == list(range(0, 4)) + list(range(10, 20))
+    report = c.storage_report()
+    assert report["attention_mode"] == "focus" and report["visible_segment_ids"] == [0, 2, 3]
+    assert [s["mode"] for s in report["segments"]] == ["fp16", "evicted", "fp16", "fp16"]
+
+
+def test_apply_plan_validates_before_changing_anything(cpu_cache):
+    c = cpu_cache
+    c.protect_segment(0)
+    plan = akv.CachePlan(tuple(akv.PlannedSegment(i, m, 0, 0.0, "t") for i, m in
+                               enumerate([CacheMode.INT4, CacheMode.INT4, CacheMode.INT8, CacheMode.FP16])),
+                         1, 0, 0)
+    with pytest.raises(ValueError, match="protected"):
+        c.apply_plan(plan)
+    assert [c.segment_mode(i) for i in range(4)] == [CacheMode.FP16] * 4
+
+
+def test_cpu_tensors_are_refused_by_the_kernels():
+    with pytest.raises(ValueError, match="CUDA"):
+        akv.quantize_tensor(torch.randn(4, 8), CacheMode.INT8, group_size=16)
+    with pytest.raises(ValueError, match="CUDA"):
+        akv.pack_page(torch.randn(2, 16, 64), 4)
