@@ -1,0 +1,375 @@
+#!/usr/bin/env python
+"""Benchmark of the packed mixed-precision KV decode path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload batched]
+
+A step is one decode token for every sequence of the batch through all layers:
+per layer, the paged split-K decode kernel and the LSE merge kernel over that
+layer's page table (one launch each).  The default workload is the batched
+Qwen3-0.6B attention shape: 28 layers, 16 query / 8 KV heads, head_dim 128,
+batch 64, 8192-token context in 16-token pages; per page FP16 / INT8 / INT4 /
+evicted = 15 / 35 / 40 / 10 %, per-block-per-KV-head fp16 scales, the page
+tables a random permutation of one shared physical pool, split-K 8, fp16
+N(0, 1) inputs (synthetic, seeded).  Under torchrun every rank decodes its
+own batch of 64 sequences (weak scaling, no collective on the data path).
+
+value: resident-KV GB/s of the whole job (algorithmic bytes: non-evicted page
+payload + scales, plus queries and outputs, divided by the max-over-ranks
+device time per step); the KV pool (25.6 GB per GPU) is far larger than L2,
+so every step reads HBM.  e2e: the same metric through the public Python
+entry point with the step's queries copied from pinned host memory and the
+outputs read back inside the timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT / "dynamic-quantization_b200"), str(ROOT)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "decode-attn resident-KV GB/s (% B200 HBM peak) & tokens/s at 1/2/4/8 GPUs"
+FALLBACK_HBM_GBS = 6650.0
+
+WORKLOADS = {
+    "batched": dict(
+        name="batched decode, Qwen3-0.6B attention shape",
+        layers=28, q_heads=16, kv_heads=8, dim=128, batch=64, tokens=8192,
+        mix={16: 0.15, 8: 0.35, 4: 0.40, 0: 0.10}, splits=8, group=2048),
+    # Same shape, 2 layers x 16 sequences (228 MB of KV per layer, > L2): the
+    # case ncu profiles are captured on.
+    "batched_small": dict(
+        name="batched decode, Qwen3-0.6B attention shape, 2 layers x 16 sequences (profiling case)",
+        layers=2, q_heads=16, kv_heads=8, dim=128, batch=16, tokens=8192,
+        mix={16: 0.15, 8: 0.35, 4: 0.40, 0: 0.10}, splits=8, group=2048),
+}
+
+
+def hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_from_profile(workload: str):
+    """DRAM bytes per decode launch from the committed ncu summary, if present."""
+    f = ROOT / "profiles" / f"decode_partials_{workload}.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi SM clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.count(",") >= 5]
+        os.unlink(self.file.name)
+        if not rows:
+            return None
+        sm = [float(r[0]) for r in rows if r[0].strip().replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[2 + i] and "Not" not in r[2 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------- CPU baseline
+def cpu_baseline(wl: dict, seed: int, seconds: float, calls_min: int = 3):
+    """Time the reference's CPU decode path (restated with torch CPU ops) on one
+    sequence-layer of the workload for about ``seconds``; returns a dict."""
+    import torch
+
+    from oracle import baseline as OB
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    blocks = wl["tokens"] // 16
+    bits = OB.random_bits(seed, blocks, wl["mix"])
+    pages = OB.build_sequence(seed, wl["kv_heads"], wl["dim"], blocks, bits, wl["group"])
+    q = torch.randn(1, wl["q_heads"], 1, wl["dim"], generator=torch.Generator().manual_seed(seed)).half()
+    scale = 1 / math.sqrt(wl["dim"])
+    OB.decode_cpu(pages, q, scale)  # warm
+    times = []
+    t_end = time.perf_counter() + seconds
+    while len(times) < calls_min or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        OB.decode_cpu(pages, q, scale)
+        times.append(time.perf_counter() - t0)
+    per_call = statistics.median(times)
+    nbytes = OB.resident_bytes(pages) + 2 * q.numel() * 2
+    calls_per_step = wl["layers"] * wl["batch"]
+    return {
+        "gbs": nbytes / per_call / 1e9,
+        "tokens_per_s": wl["batch"] / (per_call * calls_per_step),
+        "cores": cores,
+        "calls": len(times),
+        "seconds_per_call": per_call,
+        "sample": (f"{len(times)} decode calls of one sequence-layer ({blocks} pages, "
+                   f"{wl['kv_heads']} KV heads, same precision mix), median per call; "
+                   f"tokens/s extrapolated x{calls_per_step} calls per step"),
+    }
+
+
+# ------------------------------------------------------------------ GPU setup
+def build_workload(wl: dict, device, seed: int):
+    import numpy as np
+    import torch
+
+    from anchorkv_b200 import pool as P
+
+    rng = np.random.default_rng(seed)
+    nblk = wl["tokens"] // 16
+    keys = list(wl["mix"])
+    probs = np.array([wl["mix"][k] for k in keys])
+    bits = [rng.choice(np.array(keys), size=(wl["batch"], nblk), p=probs) for _ in range(wl["layers"])]
+    counts = {b: int(sum((x == b).sum() for x in bits)) for b in (16, 8, 4)}
+    pool = P.PagePool(wl["kv_heads"], wl["dim"], group=wl["group"], pages=counts, device=device,
+                      shuffle_seed=seed, zero=False)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    shape = (wl["batch"], wl["kv_heads"], wl["tokens"], wl["dim"])
+    k = torch.empty(shape, dtype=torch.float16, device=device)
+    v = torch.empty_like(k)
+    layers = []
+    for layer_bits in bits:
+        k.normal_(generator=gen)
+        v.normal_(generator=gen)
+        layers.append(P.pack_dense(pool, k, v, layer_bits, semantics="tensor"))
+    del k, v
+    q = torch.randn((wl["layers"], wl["batch"], wl["q_heads"], 1, wl["dim"]), generator=gen,
+                    device=device, dtype=torch.float32).half()
+    torch.cuda.synchronize(device)
+    kv_bytes = [t.resident_bytes() for t in layers]
+    return pool, layers, q, kv_bytes
+
+
+def run_ours(args, wl):
+    import torch
+    import torch.distributed as dist
+
+    import anchorkv_b200 as akv
+    from anchorkv_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    pool, layers, q, kv_bytes = build_workload(wl, device, seed=1234 + rank)
+    L, B, Hq, D = wl["layers"], wl["batch"], wl["q_heads"], wl["dim"]
+    splits, scale = wl["splits"], 1 / math.sqrt(D)
+    io_bytes = q[0].numel() * 2 * 2  # queries in + outputs out, per layer
+    step_bytes = sum(kv_bytes) + L * io_bytes
+    out = torch.empty_like(q)
+    parts = torch.empty((B, Hq, splits, D + 2), dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+    sptr = stream.cuda_stream
+    status = _lib.status_word(device)
+    lib = _lib.load()
+
+    def decode(l):
+        t = layers[l]
+        return lib.akv_decode_partials(pool.arena.data_ptr(), pool.nbytes, t.table.data_ptr(), t.table.stride(0),
+                                       t.seq_blocks.data_ptr(), t.max_blocks, q[l].data_ptr(), q[l].stride(0),
+                                       q[l].stride(1), B, Hq, wl["kv_heads"], D, wl["group"], scale, splits,
+                                       parts.data_ptr(), status.data_ptr(), sptr)
+
+    def merge(l):
+        return lib.akv_merge(parts.data_ptr(), B, Hq, splits, D, out[l].data_ptr(), out[l].stride(0),
+                             out[l].stride(1), None, sptr)
+
+    def step(events=None, i=0):
+        for l in range(L):
+            if events is not None:
+                events[0][i * L + l].record(stream)
+            assert decode(l) == 0
+            if events is not None:
+                events[1][i * L + l].record(stream)
+            assert merge(l) == 0
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    ev = ([torch.cuda.Event(enable_timing=True) for _ in range(args.steps * L)],
+          [torch.cuda.Event(enable_timing=True) for _ in range(args.steps * L)])
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gpu_id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    sampler = ClockSampler(gpu_id)
+    time.sleep(0.3)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(ev, i)
+    t1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    ms_local = t0.elapsed_time(t1) / args.steps
+    dec_ms = [a.elapsed_time(b) for a, b in zip(*ev)]
+    dec_ms_mean = sum(dec_ms) / len(dec_ms)
+    assert akv.take_device_status(device) == 0, "device status word set during the timed region"
+
+    # ---- end to end through the public API, pinned host buffers
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    q_dev = torch.empty_like(q)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        for l in range(L):
+            akv.packed_attention(q_dev[l], layers[l], scale, splits=splits, out=out[l])
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(10, args.steps // 4)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms_local = e0.elapsed_time(e1) / e2e_steps
+
+    times = torch.tensor([ms_local, e2e_ms_local, dec_ms_mean], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, dec_ms_max = times.tolist()
+    peak, peak_kind = hbm_peak()
+    if rank == 0:
+        total_bytes = step_bytes * world
+        gbs = total_bytes / (ms * 1e-3) / 1e9
+        tokens = B * world / (ms * 1e-3)
+        achieved = (step_bytes / L) / (dec_ms_mean * 1e-3) / 1e9
+        traffic = traffic_from_profile(args.workload)
+        line = {
+            "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 operands, f32 accumulation", "data": "synthetic (seeded fp16 N(0,1))",
+            "config": {
+                "workload": wl["name"], "layers": L, "q_heads": Hq, "kv_heads": wl["kv_heads"],
+                "head_dim": D, "batch_per_gpu": B, "context_tokens": wl["tokens"], "page_tokens": 16,
+                "precision_mix": {"fp16": wl["mix"][16], "int8": wl["mix"][8], "int4": wl["mix"][4],
+                                  "evicted": wl["mix"][0]},
+                "scale_group": wl["group"], "split_k": splits,
+                "kv_pool_gb_per_gpu": round(pool.nbytes / 1e9, 2),
+                "parallelism": f"batch-sharded x{world} (independent sequences, no collective)",
+                "l2": "inputs larger than L2 (KV pool >> 126 MB), no flush needed",
+            },
+            "tokens_per_s": round(tokens, 1),
+            "pct_of_hbm_peak": round(100 * gbs / world / peak, 2),
+            "resident_bytes_per_step_per_gpu": step_bytes,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                         "kernel": "decode_partials_kernel<128>",
+                         "traffic": traffic, "algorithmic_bytes_per_launch": step_bytes // L,
+                         "launch_ms_mean": round(dec_ms_mean, 5), "launch_ms_max_over_ranks": round(dec_ms_max, 5)},
+            "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "ms_per_step": round(e2e_ms, 4), "tokens_per_s": round(B * world / (e2e_ms * 1e-3), 1),
+                    "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
+                    "path": "anchorkv_b200.packed_attention per layer, pinned host queries/outputs"},
+            "gpu_launches": args.steps * L * 2,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            cb = cpu_baseline(wl, seed=99, seconds=args.cpu_seconds)
+            line["cpu_baseline"] = {"value": round(cb["gbs"], 4), "unit": "GB/s", "cores": cb["cores"],
+                                    "kind": "port", "sample": cb["sample"],
+                                    "tokens_per_s": round(cb["tokens_per_s"], 4)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    per_step = max(0.02, args.cpu_seconds / max(1, args.steps))
+    cb = cpu_baseline(wl, seed=99, seconds=per_step * args.steps, calls_min=args.steps + args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(cb["gbs"], 4), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(cb["seconds_per_call"] * wl["layers"] * wl["batch"] * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 operands (torch CPU SDPA)", "data": "synthetic (seeded fp16 N(0,1))",
+        "config": {"workload": wl["name"], "layers": wl["layers"], "q_heads": wl["q_heads"],
+                   "kv_heads": wl["kv_heads"], "head_dim": wl["dim"], "batch_per_gpu": wl["batch"],
+                   "context_tokens": wl["tokens"], "scale_group": wl["group"]},
+        "tokens_per_s": round(cb["tokens_per_s"], 4),
+        "cpu_baseline": {"value": round(cb["gbs"], 4), "unit": "GB/s", "cores": cb["cores"], "kind": "port",
+                         "sample": cb["sample"]},
+        "e2e": {"value": round(cb["gbs"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="batched")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()
