@@ -45,6 +45,10 @@ PROTOTYPES = {
     "akv_packed_attention": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, _c_p, _i32, _c_p, _i64, _i64,
                                             _i32, _i32, _i32, _i32, _i32, _f32, _i32, _c_p, _i64,
                                             _i64, _c_p, _i64, _c_p, _c_p]),
+    "akv_packed_attention_static": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, _c_p, _i32, _c_p, _i64, _i64,
+                                                   _i32, _i32, _i32, _i32, _i32, _f32, _i32, _c_p, _i64,
+                                                   _i64, _c_p, _c_p]),
+    "akv_static_scratch_bytes": (_i64, []),
 }
 
 

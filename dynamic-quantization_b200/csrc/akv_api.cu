@@ -7,6 +7,9 @@ extern "C" const char *akv_status_string(int status) {
     case AKV_ERR_INVALID: return "invalid argument (null pointer, size, alignment or dtype)";
     case AKV_ERR_UNSUPPORTED: return "unsupported geometry (head_dim must be 64 or 128; group a supported power of two)";
     case AKV_ERR_CUDA: return "CUDA launch error";
+    case AKV_ERR_SCRATCH:
+      return "request exceeds the fixed 8 MiB scratch of akv_packed_attention_static "
+             "(batch * q_heads * splits * (head_dim + 2) * 4 bytes); use akv_packed_attention";
     default: return "unknown status";
   }
 }

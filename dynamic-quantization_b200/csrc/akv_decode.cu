@@ -580,3 +580,60 @@ extern "C" int akv_packed_attention(const void *arena, int64_t arena_bytes, cons
   return akv_merge((const float *)workspace, batch, q_heads, splits, head_dim, out, out_batch_stride,
                    out_head_stride, nullptr, stream);
 }
+
+// ===================================================== allocation-free variant
+// akv_packed_attention_static: the same decode + merge, with the split-K
+// partials in a fixed array compiled into this library instead of a workspace
+// the caller allocates.  For callers that cannot allocate device memory: hosts
+// that reserve all of HBM up front for their own pool (a serving engine's KV
+// pool), latency-critical decode loops where cudaMalloc/cudaFree would
+// synchronize the device, and bindings that hold raw pointers but no allocator.
+//
+// Every GPU that loads the library holds the array (kStaticScratchBytes) until
+// the process exits.  All calls on a device share it and it keeps the last
+// call's contents: each call rewrites every partial it reads before reading
+// it, so nothing needs clearing, but calls whose kernels overlap on the GPU
+// (different streams without ordering between them) race on it.
+namespace akv {
+constexpr int64_t kStaticScratchBytes = 8ll << 20;  // 8 MiB per GPU
+static __device__ __align__(256) float g_static_partials[kStaticScratchBytes / sizeof(float)];
+}  // namespace akv
+
+#include <mutex>
+
+namespace {
+std::mutex g_static_mu;
+void *g_static_ptr[256];  // device address of g_static_partials, per device ordinal
+}  // namespace
+
+extern "C" int64_t akv_static_scratch_bytes(void) { return akv::kStaticScratchBytes; }
+
+extern "C" int akv_packed_attention_static(const void *arena, int64_t arena_bytes, const int64_t *table,
+                                           int64_t table_stride, const int32_t *seq_blocks,
+                                           int32_t max_blocks, const void *query, int64_t q_batch_stride,
+                                           int64_t q_head_stride, int32_t batch, int32_t q_heads,
+                                           int32_t kv_heads, int32_t head_dim, int32_t group, float scale,
+                                           int32_t splits, void *out, int64_t out_batch_stride,
+                                           int64_t out_head_stride, int32_t *dev_status, void *stream) {
+  if (!out) return AKV_ERR_INVALID;
+  const int64_t need = akv_workspace_bytes(batch, q_heads, splits, head_dim);
+  if (need <= 0) return AKV_ERR_INVALID;
+  if (need > akv::kStaticScratchBytes) return AKV_ERR_SCRATCH;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return AKV_ERR_CUDA;
+  void *scratch = nullptr;
+  {
+    // First call on a device: look up the array's device address with that device current.
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_ptr[dev]) {
+      void *p = nullptr;
+      if (cudaGetSymbolAddress(&p, akv::g_static_partials) != cudaSuccess || !p) return AKV_ERR_CUDA;
+      g_static_ptr[dev] = p;
+    }
+    scratch = g_static_ptr[dev];
+  }
+  return akv_packed_attention(arena, arena_bytes, table, table_stride, seq_blocks, max_blocks, query,
+                              q_batch_stride, q_head_stride, batch, q_heads, kv_heads, head_dim, group,
+                              scale, splits, out, out_batch_stride, out_head_stride, scratch, need,
+                              dev_status, stream);
+}

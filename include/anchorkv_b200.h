@@ -5,8 +5,9 @@
  * (passed as void*, a cudaStream_t; NULL means the legacy default stream),
  * returns an int status (AKV_OK on success), launches asynchronously on that
  * stream and allocates nothing: the caller owns every buffer, including the
- * split-K workspace.  The library keeps no mutable global state, so concurrent
- * calls on different streams are independent.
+ * split-K workspace.  Apart from the fixed scratch of
+ * akv_packed_attention_static (see its declaration), the library keeps no
+ * mutable global state, so concurrent calls on different streams are independent.
  *
  * Reference interfaces each entry point replaces are cited by file:line in
  * the reference project (Dev-Sinha13/Dynamic-Quantization, src/anchorkv/).
@@ -39,6 +40,7 @@ extern "C" {
 #define AKV_ERR_INVALID 1     /* bad argument: null pointer, size, alignment, dtype */
 #define AKV_ERR_UNSUPPORTED 2 /* well-formed but unsupported geometry */
 #define AKV_ERR_CUDA 3        /* CUDA error when launching */
+#define AKV_ERR_SCRATCH 4     /* request larger than akv_packed_attention_static's fixed scratch */
 
 /* Bits a kernel ORs into the optional device status word (int32, caller owned). */
 #define AKV_DEV_BAD_DESCRIPTOR 1 /* descriptor outside the arena or misaligned; page skipped */
@@ -149,6 +151,30 @@ int akv_packed_attention(const void *arena, int64_t arena_bytes, const int64_t *
                          int32_t group, float scale, int32_t splits, void *out,
                          int64_t out_batch_stride, int64_t out_head_stride, void *workspace,
                          int64_t workspace_bytes, int32_t *dev_status, void *stream);
+
+/* Allocation-free akv_packed_attention.  No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory -- hosts that reserve
+ * all of HBM for their own pool, latency-critical loops where cudaMalloc/cudaFree
+ * would synchronize the device, bindings holding raw pointers but no allocator.
+ * The split-K partials live in a fixed array inside the library
+ * (akv_static_scratch_bytes() = 8 MiB per GPU, held until process exit), so it
+ * allocates nothing; requests needing more than that
+ * (batch * q_heads * splits * (head_dim + 2) * 4 bytes) return AKV_ERR_SCRATCH.
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture.  All calls on a device share the array and it keeps the
+ * last call's contents (each call rewrites what it reads, so nothing needs
+ * clearing); calls whose kernels overlap on the GPU race on it. */
+int akv_packed_attention_static(const void *arena, int64_t arena_bytes, const int64_t *table,
+                                int64_t table_stride, const int32_t *seq_blocks, int32_t max_blocks,
+                                const void *query, int64_t q_batch_stride, int64_t q_head_stride,
+                                int32_t batch, int32_t q_heads, int32_t kv_heads, int32_t head_dim,
+                                int32_t group, float scale, int32_t splits, void *out,
+                                int64_t out_batch_stride, int64_t out_head_stride,
+                                int32_t *dev_status, void *stream);
+
+/* Size in bytes of the fixed scratch akv_packed_attention_static uses (8 MiB). */
+int64_t akv_static_scratch_bytes(void);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,87 @@
+"""akv_packed_attention_static, the allocation-free decode entry point, through the C ABI.
+
+Some callers cannot allocate device memory: hosts that reserve all of HBM up
+front for their own pool (a serving engine's KV pool), latency-critical decode
+loops where cudaMalloc/cudaFree would synchronize the device, and bindings that
+hold raw pointers but no allocator.  For them the split-K partials live in a
+fixed 8 MiB array inside the library.  This file checks, on two calls in a row,
+that its output matches akv_packed_attention with a caller-owned workspace
+(within the decode tolerance), and that oversize requests are refused.  It is
+named so pytest collects it last.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import workloads as W
+from anchorkv_b200 import _lib
+from anchorkv_b200 import pool as P
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def _store(cuda, seed, batch, q_heads, kv_heads, tokens, group):
+    k = W.outlier_kv(seed, (batch, kv_heads, tokens, 128))
+    v = W.outlier_kv(seed + 1, (batch, kv_heads, tokens, 128))
+    q = W.normal(seed + 2, (batch, q_heads, 1, 128)).to(cuda)
+    nblk = tokens // 16
+    bits = np.array(W.draw_modes(seed + 3, batch * nblk, {16: .15, 8: .35, 4: .4, 0: .1})).reshape(batch, nblk)
+    pool = P.PagePool(kv_heads, 128, group=group, pages={b: int((bits == b).sum()) for b in (16, 8, 4)},
+                      device=cuda, shuffle_seed=seed)
+    return q, P.pack_dense(pool, k.to(cuda), v.to(cuda), bits, semantics="tensor" if group == 2048 else "page")
+
+
+def _args(q, store, splits):
+    pool, t = store.pool, store.table
+    return (pool.arena.data_ptr(), pool.nbytes, t.data_ptr(), t.stride(0), store.seq_blocks.data_ptr(),
+            store.max_blocks, q.data_ptr(), q.stride(0), q.stride(1), q.shape[0], q.shape[1], pool.heads,
+            128, pool.group, 1 / math.sqrt(128), splits)
+
+
+def _with_workspace(q, store, splits, cuda):
+    lib = _lib.load()
+    out = torch.empty_like(q)
+    ws = torch.empty(lib.akv_workspace_bytes(q.shape[0], q.shape[1], splits, 128), dtype=torch.uint8, device=cuda)
+    status = lib.akv_packed_attention(*_args(q, store, splits), out.data_ptr(), out.stride(0), out.stride(1),
+                                      ws.data_ptr(), ws.numel(), None, _lib.stream_of(cuda))
+    assert status == _lib.OK, _lib.status_string(status)
+    return out
+
+
+def _static(q, store, splits, cuda):
+    lib = _lib.load()
+    out = torch.empty_like(q)
+    status = lib.akv_packed_attention_static(*_args(q, store, splits), out.data_ptr(), out.stride(0),
+                                             out.stride(1), None, _lib.stream_of(cuda))
+    assert status == _lib.OK, _lib.status_string(status)
+    return out
+
+
+def test_static_scratch_matches_workspace_entry_on_consecutive_calls(cuda):
+    first = _store(cuda, 501, batch=4, q_heads=16, kv_heads=8, tokens=1024, group=2048)
+    second = _store(cuda, 601, batch=2, q_heads=32, kv_heads=8, tokens=512, group=64)
+    static_first = _static(*first, 8, cuda)
+    static_second = _static(*second, 3, cuda)  # reuses the scratch the first call left behind
+    torch.cuda.synchronize(cuda)
+    for (q, store), splits, got in ((first, 8, static_first), (second, 3, static_second)):
+        want = _with_workspace(q, store, splits, cuda)
+        np.testing.assert_allclose(got.float().cpu().numpy(), want.float().cpu().numpy(), atol=ATOL, rtol=RTOL)
+    again = _static(*first, 8, cuda)
+    np.testing.assert_allclose(again.float().cpu().numpy(), static_first.float().cpu().numpy(),
+                               atol=ATOL, rtol=RTOL)
+
+
+def test_static_scratch_refuses_requests_beyond_its_size(cuda):
+    lib = _lib.load()
+    assert lib.akv_static_scratch_bytes() == 8 << 20
+    q, store = _store(cuda, 701, batch=1, q_heads=16, kv_heads=8, tokens=64, group=2048)
+    splits = (8 << 20) // (16 * 130 * 4) + 1  # one split more than the scratch holds
+    out = torch.empty_like(q)
+    status = lib.akv_packed_attention_static(*_args(q, store, splits), out.data_ptr(), out.stride(0),
+                                             out.stride(1), None, _lib.stream_of(cuda))
+    assert status == 4  # AKV_ERR_SCRATCH
+    assert "8 MiB" in _lib.status_string(status)
