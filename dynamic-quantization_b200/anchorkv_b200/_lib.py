@@ -13,7 +13,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "lib" / "libanchorkv_b200.so"
 
-OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_SCRATCH = 0, 1, 2, 3, 4
 DEV_BAD_DESCRIPTOR, DEV_TIMEOUT = 1, 2
 MODE_SKIP, MODE_INT4, MODE_INT8, MODE_FP16 = 0, 1, 2, 3
 SEM_TENSOR, SEM_PAGE = 0, 1
@@ -38,10 +38,12 @@ PROTOTYPES = {
                                         ctypes.c_int, _c_p, _c_p]),
     "akv_unpack_pages": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_int, _c_p, _c_p, _c_p, _c_p]),
-    "akv_workspace_bytes": (_i64, [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "akv_workspace_bytes": (_i64, [ctypes.c_int] * 6),
     "akv_decode_partials": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, _c_p, _i32, _c_p, _i64, _i64,
-                                           _i32, _i32, _i32, _i32, _i32, _f32, _i32, _c_p, _c_p, _c_p]),
-    "akv_merge": (ctypes.c_int, [_c_p, _i32, _i32, _i32, _i32, _c_p, _i64, _i64, _c_p, _c_p]),
+                                           _i32, _i32, _i32, _i32, _i32, _f32, _i32, _c_p, _i64, _c_p,
+                                           _c_p]),
+    "akv_merge": (ctypes.c_int, [_c_p, _i32, _i32, _i32, _c_p, _i64, _i64, _c_p, _c_p, _c_p]),
+    "akv_merge_states": (ctypes.c_int, [_c_p, _i32, _i32, _i32, _i32, _c_p, _i64, _i64, _c_p]),
     "akv_packed_attention": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, _c_p, _i32, _c_p, _i64, _i64,
                                             _i32, _i32, _i32, _i32, _i32, _f32, _i32, _c_p, _i64,
                                             _i64, _c_p, _i64, _c_p, _c_p]),

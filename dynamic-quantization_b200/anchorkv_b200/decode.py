@@ -6,9 +6,10 @@ It also accepts a :class:`~anchorkv_b200.pool.PagedBatch` (batch of sequences
 over a shared page pool), where the query is ``[batch, Hq, 1, D]``.
 
 The work runs in two sm_100a kernels behind the C ABI (akv_packed_attention):
-the paged split-K decode (one CTA per split x KV head x sequence, bulk-copied
-pages, register dequantisation into mma.sync fragments, fp32 online softmax)
-and the log-sum-exp merge.
+the paged decode (persistent stream-K: every resident warp takes a contiguous
+range of (sequence, KV head, page) work, bulk-copies the pages into a private
+shared-memory ring, dequantises in registers into mma.sync fragments and keeps
+an fp32 online softmax) and the log-sum-exp merge of the partial states.
 """
 
 from __future__ import annotations
@@ -42,7 +43,9 @@ def packed_attention(query, layer, scale, splits=4, *, out=None):
     """Attend one query token per sequence over the layer's packed pages.
 
     ``query``: fp16 CUDA ``[batch, Hq, 1, D]`` (batch 1 for a PagedLayer).
-    ``splits``: split-K factor over each sequence's pages (merged by LSE).
+    ``splits``: at most this many pieces per (sequence, KV head), merged by
+    LSE (the reference's split-K knob; ``0`` lets the device use every resident
+    warp).  Results do not depend on it beyond fp32 rounding.
     """
     batched = isinstance(layer, PagedBatch)
     batch = layer.batch if batched else 1
@@ -58,15 +61,17 @@ def packed_attention(query, layer, scale, splits=4, *, out=None):
     heads = query.shape[1]
     if heads % layer.heads:
         raise ValueError('query heads must be divisible by KV heads')
-    if splits < 1:
-        raise ValueError('splits must be positive')
+    if splits < 0:
+        raise ValueError('splits must be non-negative')
     if query.stride(-1) != 1 or query.stride(1) % 8 or query.stride(0) % 8 or query.data_ptr() % 16:
         query = query.contiguous()
     arena, arena_bytes, table, seq_blocks, max_blocks = _store_geometry(layer)
     if out is None:
         out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
     dev = query.device
-    nbytes = _lib.load().akv_workspace_bytes(batch, heads, splits, layer.dim)
+    nbytes = _lib.load().akv_workspace_bytes(batch, heads, layer.heads, layer.dim, max_blocks, splits)
+    if nbytes < 0:
+        raise ValueError('unsupported decode geometry')
     ws = _workspace(dev, nbytes)
     _lib.call("akv_packed_attention", arena.data_ptr(), arena_bytes, table.data_ptr(), table.stride(0),
               None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks,
@@ -76,38 +81,40 @@ def packed_attention(query, layer, scale, splits=4, *, out=None):
     return out
 
 
-def decode_partial_states(query, layer, scale, splits=4):
-    """Split-K decode merged to one LSE state per (sequence, query head).
+def decode_partial_states(query, layer, scale, splits=0):
+    """Decode merged to one LSE state per (sequence, query head).
 
     Returns fp32 ``[batch, Hq, D + 2]`` = (acc[D], m, l) with ``m`` in base-2
-    units of the scaled score, for a further merge (e.g. across GPUs) with
-    :func:`merge_states`."""
+    units of the scaled score, for a further merge (e.g. across GPUs holding
+    contiguous shards of each sequence) with :func:`merge_states`."""
     batched = isinstance(layer, PagedBatch)
     batch = layer.batch if batched else 1
     heads = query.shape[1]
     query = query.contiguous()
     arena, arena_bytes, table, seq_blocks, max_blocks = _store_geometry(layer)
     dev = query.device
-    parts = torch.empty((batch, heads, splits, layer.dim + 2), dtype=torch.float32, device=dev)
+    nbytes = _lib.load().akv_workspace_bytes(batch, heads, layer.heads, layer.dim, max_blocks, splits)
+    if nbytes < 0:
+        raise ValueError('unsupported decode geometry')
+    ws = _workspace(dev, nbytes)
     state = torch.empty((batch, heads, layer.dim + 2), dtype=torch.float32, device=dev)
     stream = _lib.stream_of(dev)
+    status = _lib.status_word(dev).data_ptr()
     _lib.call("akv_decode_partials", arena.data_ptr(), arena_bytes, table.data_ptr(), table.stride(0),
               None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks, query.data_ptr(),
               query.stride(0), query.stride(1), batch, heads, layer.heads, layer.dim, layer.group,
-              float(scale), splits, parts.data_ptr(), _lib.status_word(dev).data_ptr(), stream)
-    _lib.call("akv_merge", parts.data_ptr(), batch, heads, splits, layer.dim, None, 0, 0,
-              state.data_ptr(), stream)
+              float(scale), splits, ws.data_ptr(), ws.numel(), status, stream)
+    _lib.call("akv_merge", ws.data_ptr(), batch, heads, layer.dim, None, 0, 0, state.data_ptr(), status,
+              stream)
     return state
 
 
-def merge_states(states: torch.Tensor, *, out_dtype=torch.float16) -> torch.Tensor:
+def merge_states(states: torch.Tensor) -> torch.Tensor:
     """Merge ``[n, batch, Hq, D + 2]`` LSE states (e.g. gathered from n GPUs)
-    into the normalised output ``[batch, Hq, 1, D]``."""
+    into the normalised fp16 output ``[batch, Hq, 1, D]``."""
     n, batch, heads, rs = states.shape
-    dim = rs - 2
-    # akv_merge expects [batch][heads][splits][D+2]
-    parts = states.permute(1, 2, 0, 3).contiguous()
-    out = torch.empty((batch, heads, 1, dim), dtype=torch.float16, device=states.device)
-    _lib.call("akv_merge", parts.data_ptr(), batch, heads, n, dim, out.data_ptr(), out.stride(0),
-              out.stride(1), None, _lib.stream_of(states.device))
-    return out if out_dtype == torch.float16 else out.to(out_dtype)
+    states = states.contiguous()
+    out = torch.empty((batch, heads, 1, rs - 2), dtype=torch.float16, device=states.device)
+    _lib.call("akv_merge_states", states.data_ptr(), n, batch, heads, rs - 2, out.data_ptr(),
+              out.stride(0), out.stride(1), _lib.stream_of(states.device))
+    return out

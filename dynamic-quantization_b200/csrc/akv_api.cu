@@ -9,12 +9,12 @@ extern "C" const char *akv_status_string(int status) {
     case AKV_ERR_CUDA: return "CUDA launch error";
     case AKV_ERR_SCRATCH:
       return "request exceeds the fixed 8 MiB scratch of akv_packed_attention_static "
-             "(batch * q_heads * splits * (head_dim + 2) * 4 bytes); use akv_packed_attention";
+             "(akv_workspace_bytes of the call); use akv_packed_attention with a workspace";
     default: return "unknown status";
   }
 }
 
-extern "C" int akv_abi_version(void) { return 1; }
+extern "C" int akv_abi_version(void) { return 2; }
 
 extern "C" int64_t akv_record_bytes(int head_dim, int group, int mode) {
   if (head_dim <= 0 || group <= 0 || (16 * head_dim) % group) return -1;

@@ -1,30 +1,41 @@
-// Paged split-K decode attention over mixed FP16/INT8/INT4 pages, and the
-// log-sum-exp merge of its partial states.
+// Paged decode attention over mixed FP16/INT8/INT4 pages (persistent stream-K),
+// and the log-sum-exp merge of its partial states.
 //
 // Reference: src/anchorkv/triton_decode.py:35-104 (one program per (query head,
 // split), pages strided across splits, fp32 online softmax, fp16 rounding of
 // dequantised values, LSE merge), whose numerics it reproduces with a
 // different execution plan:
 //
-//  * one CTA per (split, KV head, sequence) serves every query head of that KV
-//    head (the reference re-reads each KV page once per query head);
-//  * each of the CTA's 4 warps streams its share of the split's pages through a
-//    private 16 KB shared-memory ring with bulk copies (cp.async.bulk, mbarrier
-//    completion, no multicast; one elected lane issues), skipping evicted or
-//    invisible pages without reading them;
+//  * work is the flattened space of (sequence, KV head, query-head group, page)
+//    items; every resident warp takes one contiguous range of it (stream-K), so
+//    the load is balanced at page granularity and a warp's bulk-copy pipeline
+//    stays full across sequence boundaries;
+//  * each warp streams its own pages: it turns 32 page descriptors at a time
+//    into ready records lane-parallel (one lane per page, descriptor loads a
+//    window ahead, a ballot marks the pages to copy), skips evicted or
+//    invisible pages without reading them, and bulk-copies each record
+//    (cp.async.bulk, mbarrier completion, no multicast; lane 0 issues) into a
+//    private 16 KB shared-memory ring the moment it frees room, so the copy
+//    pipeline needs no hand-off between warps;
+//  * a warp serves every query head of its KV head (up to 8 per pass; the
+//    reference re-reads each KV page once per query head);
 //  * a page's K/V are dequantised in registers straight into tensor-core
 //    fragments (exact: the integer is formed in fp16 by an exponent trick and
 //    multiplied by the fp16 scale with one rounding, matching
 //    fp16(int * float(scale)) of packed_decode.py:45 / triton_decode.py:31);
 //  * Q.K^T and P.V run as mma.sync m16n8k16 (f16 x f16 -> f32): 16 tokens x 8
-//    query heads per page, so one page costs 2 * head_dim/16 MMAs;
-//  * the online softmax is fp32 in base 2 with warp-shuffle max reductions and
-//    lazy rescaling (the running max only moves when a page exceeds it by more
-//    than 2^8, so P stays <= 256 in fp16);
-//  * the CTA merges its warps in shared memory and writes one partial state
-//    (acc[D], m, l) per (sequence, query head, split); a second kernel merges
-//    splits (and, through akv_merge's state output, GPUs).
+//    query heads per page, 2 * head_dim/16 MMAs per page;
+//  * the online softmax is fp32 in base 2; the running max only moves (one
+//    warp vote, then a shuffle reduction) when a page exceeds it by more than
+//    2^8, so P stays <= 256 in fp16 and most pages need no reduction at all;
+//  * each warp writes one partial state (acc[D], m, l) per item it touched into
+//    the caller's workspace; the merge kernel combines the few warps that
+//    share an item.  The workspace starts with a header describing the
+//    decomposition, so merging needs nothing but the workspace.
 #include <math.h>
+
+#include <algorithm>
+#include <mutex>
 
 #include "akv_common.cuh"
 
@@ -32,16 +43,25 @@ namespace akv {
 
 template <int D>
 struct DecodeTraits {
-  static constexpr int kWarps = 4;
+  static constexpr int kWarps = 4;     // independent streaming warps per CTA
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kRing = 16384;  // bytes of ring per warp (power of two)
+  static constexpr int kCtasPerSm = 3;
+  static constexpr int kRing = 16384;  // bytes of ring per warp
   static constexpr int kSlots = 8;     // records in flight per warp
   static constexpr int DK = D / 4;     // K dims a lane owns per row
   static constexpr int DV = D / 8;     // V dims a lane owns per row
   static constexpr int kTiles = D / 16;
   static constexpr int kSmem = kWarps * kRing + kWarps * kSlots * (8 + 4 + 4);
-  static_assert(kWarps * 8 * (D + 2) * 4 <= kWarps * kRing, "merge scratch must fit in the rings");
+  static_assert(kRing % 16 == 0 && kRing >= 4 * kBlock * D, "a ring must hold one FP16 record");
 };
+
+// Workspace header (int32 words), written by the decode kernel, read by merge.
+enum HeaderField {
+  kMagic, kWarpsF, kSmaxF, kRangeF, kMaxBlocksF, kItemsF, kKvHeadsF, kQGroupsF, kGqaF,
+  kHeadDimF, kSlotHeadsF, kQHeadsF, kBatchF, kHeaderWords
+};
+constexpr int32_t kHeaderMagic = 0x414b5632;  // "AKV2"
+constexpr int64_t kHeaderBytes = 256;
 
 struct DecodeParams {
   const uint8_t *arena;
@@ -52,8 +72,10 @@ struct DecodeParams {
   int32_t max_blocks;
   const __half *q;
   int64_t q_bs, q_hs;
-  int32_t q_heads, kv_heads, gqa, qgroups, splits, chunk, log2_group;
+  int32_t batch, q_heads, kv_heads, gqa, qgroups, items, log2_group;
+  int32_t warps, range, smax, slot_heads;
   float scale_log2;
+  int32_t *header;
   float *partials;
   int32_t *status;
 };
@@ -97,8 +119,9 @@ struct ScaleIdx {
 // query heads 2t4, 2t4+1.  The contraction dim is permuted identically in the
 // K (A) and Q (B) fragments: k16 chunk c = 2j + hb takes, from the lane's 8-dim
 // word group j, dims {2hb, 2hb+4} (fragment cols 2t4, 2t4+1) and
-// {2hb+1, 2hb+5} (cols 2t4+8, 2t4+9).
-template <int D, int MODE>
+// {2hb+1, 2hb+5} (cols 2t4+8, 2t4+9).  Even and odd chunks accumulate into
+// separate tiles so the MMA dependency chain is half as long.
+template <int D, int MODE, bool SLAB>
 __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, const ScaleIdx &si,
                                         int gid, int t4, const uint32_t (&qf)[D / 16][2],
                                         float (&s)[4]) {
@@ -106,48 +129,62 @@ __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, c
   constexpr int bits = mode_bits(MODE);
   constexpr int rowB = D * bits / 8;
   constexpr int W = T::DK * bits / 32;  // words of one row slice
-  uint32_t r0[W], r1[W];
-  lds_words<W>(rec + gid * rowB + t4 * (W * 4), r0);
-  lds_words<W>(rec + (gid + 8) * rowB + t4 * (W * 4), r1);
-  if constexpr (MODE == AKV_MODE_INT4) {
-    const uint32_t sc0 = rep_half(ksc + si.k0), sc1 = rep_half(ksc + si.k1);
+  constexpr int NJ = D / 32;            // 8-dim word groups per slice
+  constexpr int WJ = W / NJ;            // words per group (1, 2 or 4)
+  constexpr bool WHOLE = W <= 8;        // narrow slices load at once, wide ones per group
+  const uint8_t *row0 = rec + gid * rowB + t4 * (W * 4);
+  const uint8_t *row1 = row0 + 8 * rowB;
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  uint32_t sc0 = 0, sc1 = 0;
+  if constexpr (MODE != AKV_MODE_FP16) {
+    sc0 = rep_half(ksc + (SLAB ? 0 : si.k0));
+    sc1 = SLAB ? sc0 : rep_half(ksc + si.k1);
+  }
+  uint32_t a0w[WHOLE ? W : 1], a1w[WHOLE ? W : 1];
+  if constexpr (WHOLE) {
+    lds_words<W>(row0, a0w);
+    lds_words<W>(row1, a1w);
+  }
 #pragma unroll
-    for (int j = 0; j < W; ++j) {
-      uint32_t x0 = r0[j], x1 = r1[j];
+  for (int j = 0; j < NJ; ++j) {
+    uint32_t r0[WJ], r1[WJ];
+    if constexpr (WHOLE) {
+#pragma unroll
+      for (int i = 0; i < WJ; ++i) r0[i] = a0w[WJ * j + i], r1[i] = a1w[WJ * j + i];
+    } else {
+      lds_words<WJ>(row0 + 4 * WJ * j, r0);
+      lds_words<WJ>(row1 + 4 * WJ * j, r1);
+    }
+    if constexpr (MODE == AKV_MODE_INT4) {
+      uint32_t x0 = r0[0], x1 = r1[0];
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
-        mma_16816(s, hmul2(int4_lo_to_f16x2(x0), sc0), hmul2(int4_lo_to_f16x2(x1), sc1),
+        mma_16816(acc[hb], hmul2(int4_lo_to_f16x2(x0), sc0), hmul2(int4_lo_to_f16x2(x1), sc1),
                   hmul2(int4_hi_to_f16x2(x0), sc0), hmul2(int4_hi_to_f16x2(x1), sc1),
                   qf[2 * j + hb][0], qf[2 * j + hb][1]);
         x0 >>= 8, x1 >>= 8;
       }
-    }
-  } else if constexpr (MODE == AKV_MODE_INT8) {
-    const uint32_t sc0 = rep_half(ksc + si.k0), sc1 = rep_half(ksc + si.k1);
-#pragma unroll
-    for (int j = 0; j < W / 2; ++j) {
+    } else if constexpr (MODE == AKV_MODE_INT8) {
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
         const uint32_t lo = sel8(2 * hb), hi = sel8(2 * hb + 1);
-        mma_16816(s, hmul2(int8_to_f16x2(prmt(r0[2 * j], r0[2 * j + 1], lo)), sc0),
-                  hmul2(int8_to_f16x2(prmt(r1[2 * j], r1[2 * j + 1], lo)), sc1),
-                  hmul2(int8_to_f16x2(prmt(r0[2 * j], r0[2 * j + 1], hi)), sc0),
-                  hmul2(int8_to_f16x2(prmt(r1[2 * j], r1[2 * j + 1], hi)), sc1),
+        mma_16816(acc[hb], hmul2(int8_to_f16x2(prmt(r0[0], r0[1], lo)), sc0),
+                  hmul2(int8_to_f16x2(prmt(r1[0], r1[1], lo)), sc1),
+                  hmul2(int8_to_f16x2(prmt(r0[0], r0[1], hi)), sc0),
+                  hmul2(int8_to_f16x2(prmt(r1[0], r1[1], hi)), sc1),
                   qf[2 * j + hb][0], qf[2 * j + hb][1]);
       }
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < W / 4; ++j) {
+    } else {
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
-        const uint32_t a0 = r0[4 * j + hb], b0 = r0[4 * j + 2 + hb];
-        const uint32_t a1 = r1[4 * j + hb], b1 = r1[4 * j + 2 + hb];
-        mma_16816(s, prmt(a0, b0, 0x5410), prmt(a1, b1, 0x5410), prmt(a0, b0, 0x7632),
+        const uint32_t a0 = r0[hb], b0 = r0[2 + hb], a1 = r1[hb], b1 = r1[2 + hb];
+        mma_16816(acc[hb], prmt(a0, b0, 0x5410), prmt(a1, b1, 0x5410), prmt(a0, b0, 0x7632),
                   prmt(a1, b1, 0x7632), qf[2 * j + hb][0], qf[2 * j + hb][1]);
       }
     }
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) s[i] = acc[0][i] + acc[1][i];
 }
 
 // ------------------------------------------------------------------- P . V
@@ -155,54 +192,66 @@ __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, c
 // DV*gid + [0, DV): m-tile m's A rows gid / gid+8 are dims DV*gid + 2m / +2m+1;
 // its k (token) columns 2t4, 2t4+1 / 2t4+8, 2t4+9 match the P fragment that
 // movmatrix produced from the score accumulators.
-template <int D, int MODE>
+template <int D, int MODE, bool SLAB>
 __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, const ScaleIdx &si,
                                         int gid, int t4, uint32_t b0, uint32_t b1,
                                         float (&o)[D / 16][4]) {
   using T = DecodeTraits<D>;
   constexpr int bits = mode_bits(MODE);
   constexpr int rowB = D * bits / 8;
-  constexpr int W = T::DV * bits / 32;
-  uint32_t wa[W], wb[W], wc[W], wd[W];
+  constexpr int W = T::DV * bits / 32;        // words of one row slice
+  constexpr int PARTS = W >= 8 ? 2 : 1;       // load wide slices in halves (fewer live registers)
+  constexpr int WP = W / PARTS;
+  constexpr int TP = (D / 16) / PARTS;        // m-tiles per part
   const uint8_t *base = vrec + gid * (W * 4);
-  lds_words<W>(base + (2 * t4) * rowB, wa);
-  lds_words<W>(base + (2 * t4 + 1) * rowB, wb);
-  lds_words<W>(base + (2 * t4 + 8) * rowB, wc);
-  lds_words<W>(base + (2 * t4 + 9) * rowB, wd);
-  if constexpr (MODE == AKV_MODE_INT4) {
-    const uint32_t sab = pair_half(vsc + si.va, vsc + si.vb);
-    const uint32_t scd = pair_half(vsc + si.vc, vsc + si.vd);
-#pragma unroll
-    for (int q = 0; q < W; ++q) {
-      const uint32_t xab = prmt(wa[q], wb[q], 0x5410), yab = prmt(wa[q], wb[q], 0x7632);
-      const uint32_t xcd = prmt(wc[q], wd[q], 0x5410), ycd = prmt(wc[q], wd[q], 0x7632);
-#pragma unroll
-      for (int mm = 0; mm < 4; ++mm) {
-        const uint32_t ab = (mm < 2 ? xab : yab) >> (8 * (mm & 1));
-        const uint32_t cd = (mm < 2 ? xcd : ycd) >> (8 * (mm & 1));
-        mma_16816(o[4 * q + mm], hmul2(int4_lo_to_f16x2(ab), sab), hmul2(int4_hi_to_f16x2(ab), sab),
-                  hmul2(int4_lo_to_f16x2(cd), scd), hmul2(int4_hi_to_f16x2(cd), scd), b0, b1);
-      }
+  uint32_t sab = 0, scd = 0;
+  if constexpr (MODE != AKV_MODE_FP16) {
+    if constexpr (SLAB) {
+      sab = scd = rep_half(vsc);
+    } else {
+      sab = pair_half(vsc + si.va, vsc + si.vb);
+      scd = pair_half(vsc + si.vc, vsc + si.vd);
     }
-  } else if constexpr (MODE == AKV_MODE_INT8) {
-    const uint32_t sab = pair_half(vsc + si.va, vsc + si.vb);
-    const uint32_t scd = pair_half(vsc + si.vc, vsc + si.vd);
+  }
 #pragma unroll
-    for (int q = 0; q < W; ++q) {
+  for (int part = 0; part < PARTS; ++part) {
+    uint32_t wa[WP], wb[WP], wc[WP], wd[WP];
+    lds_words<WP>(base + (2 * t4) * rowB + 4 * WP * part, wa);
+    lds_words<WP>(base + (2 * t4 + 1) * rowB + 4 * WP * part, wb);
+    lds_words<WP>(base + (2 * t4 + 8) * rowB + 4 * WP * part, wc);
+    lds_words<WP>(base + (2 * t4 + 9) * rowB + 4 * WP * part, wd);
+    float(&op)[TP][4] = *reinterpret_cast<float(*)[TP][4]>(&o[TP * part][0]);
+    if constexpr (MODE == AKV_MODE_INT4) {
 #pragma unroll
-      for (int mm = 0; mm < 2; ++mm) {
-        const uint32_t lo = sel8(2 * mm), hi = sel8(2 * mm + 1);
-        mma_16816(o[2 * q + mm], hmul2(int8_to_f16x2(prmt(wa[q], wb[q], lo)), sab),
-                  hmul2(int8_to_f16x2(prmt(wa[q], wb[q], hi)), sab),
-                  hmul2(int8_to_f16x2(prmt(wc[q], wd[q], lo)), scd),
-                  hmul2(int8_to_f16x2(prmt(wc[q], wd[q], hi)), scd), b0, b1);
+      for (int q = 0; q < WP; ++q) {
+        const uint32_t xab = prmt(wa[q], wb[q], 0x5410), yab = prmt(wa[q], wb[q], 0x7632);
+        const uint32_t xcd = prmt(wc[q], wd[q], 0x5410), ycd = prmt(wc[q], wd[q], 0x7632);
+#pragma unroll
+        for (int mm = 0; mm < 4; ++mm) {
+          const uint32_t ab = (mm < 2 ? xab : yab) >> (8 * (mm & 1));
+          const uint32_t cd = (mm < 2 ? xcd : ycd) >> (8 * (mm & 1));
+          mma_16816(op[4 * q + mm], hmul2(int4_lo_to_f16x2(ab), sab), hmul2(int4_hi_to_f16x2(ab), sab),
+                    hmul2(int4_lo_to_f16x2(cd), scd), hmul2(int4_hi_to_f16x2(cd), scd), b0, b1);
+        }
       }
-    }
-  } else {
+    } else if constexpr (MODE == AKV_MODE_INT8) {
 #pragma unroll
-    for (int m = 0; m < W; ++m)
-      mma_16816(o[m], prmt(wa[m], wb[m], 0x5410), prmt(wa[m], wb[m], 0x7632),
-                prmt(wc[m], wd[m], 0x5410), prmt(wc[m], wd[m], 0x7632), b0, b1);
+      for (int q = 0; q < WP; ++q) {
+#pragma unroll
+        for (int mm = 0; mm < 2; ++mm) {
+          const uint32_t lo = sel8(2 * mm), hi = sel8(2 * mm + 1);
+          mma_16816(op[2 * q + mm], hmul2(int8_to_f16x2(prmt(wa[q], wb[q], lo)), sab),
+                    hmul2(int8_to_f16x2(prmt(wa[q], wb[q], hi)), sab),
+                    hmul2(int8_to_f16x2(prmt(wc[q], wd[q], lo)), scd),
+                    hmul2(int8_to_f16x2(prmt(wc[q], wd[q], hi)), scd), b0, b1);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < WP; ++m)
+        mma_16816(op[m], prmt(wa[m], wb[m], 0x5410), prmt(wa[m], wb[m], 0x7632),
+                  prmt(wc[m], wd[m], 0x5410), prmt(wc[m], wd[m], 0x7632), b0, b1);
+    }
   }
 }
 
@@ -220,17 +269,16 @@ __device__ __forceinline__ void page_softmax(float (&s)[4], int ntok, int gid, f
     if (gid >= ntok) s[0] = s[1] = kNegInf;
     if (gid + 8 >= ntok) s[2] = s[3] = kNegInf;
   }
-  float mx0 = fmaxf(s[0], s[2]), mx1 = fmaxf(s[1], s[3]);
+  float mx0 = fmaxf(s[0], s[2]) * scale_log2, mx1 = fmaxf(s[1], s[3]) * scale_log2;
+  // Lazy rescale: keep the running max unless some score exceeds it by > 8
+  // (P <= 2^8 in fp16 is exact enough and cannot overflow).  Only then reduce
+  // the page max across the lanes that share a head.
+  if (__any_sync(0xffffffffu, mx0 > st.m0 + 8.f || mx1 > st.m1 + 8.f)) {
 #pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-  }
-  mx0 *= scale_log2, mx1 *= scale_log2;
-  // Lazy rescale: keep the running max unless this page exceeds it by > 8
-  // (P <= 2^8 in fp16 is exact enough and cannot overflow).
-  const bool grow = mx0 > st.m0 + 8.f || mx1 > st.m1 + 8.f;
-  if (__any_sync(0xffffffffu, grow)) {
+    for (int off = 4; off < 32; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
     const float n0 = fmaxf(st.m0, mx0), n1 = fmaxf(st.m1, mx1);
     const float a0 = ex2(st.m0 - n0), a1 = ex2(st.m1 - n1);
     st.l0 *= a0, st.l1 *= a1;
@@ -247,7 +295,7 @@ __device__ __forceinline__ void page_softmax(float (&s)[4], int ntok, int gid, f
   b1 = movmatrix_trans(pack_f16x2(p2, p3));
 }
 
-template <int D, int MODE>
+template <int D, int MODE, bool SLAB>
 __device__ __forceinline__ void page_attend(uint8_t *rec, int ntok, int lane, int log2_group,
                                             const ScaleIdx &si, const uint32_t (&qf)[D / 16][2],
                                             float scale_log2, SoftmaxState &st,
@@ -262,28 +310,72 @@ __device__ __forceinline__ void page_attend(uint8_t *rec, int ntok, int lane, in
     __syncwarp();
   }
   const __half *ksc = reinterpret_cast<const __half *>(rec + 2 * PB);
-  const __half *vsc = ksc + ((kBlock * D) >> log2_group);
-  float s[4] = {0.f, 0.f, 0.f, 0.f};
-  page_qk<D, MODE>(rec, ksc, si, gid, t4, qf, s);
+  const __half *vsc = ksc + (SLAB ? 1 : ((kBlock * D) >> log2_group));
+  float s[4];
+  page_qk<D, MODE, SLAB>(rec, ksc, si, gid, t4, qf, s);
   uint32_t b0, b1;
   page_softmax<D>(s, ntok, gid, scale_log2, st, o, b0, b1);
-  page_pv<D, MODE>(rec + PB, vsc, si, gid, t4, b0, b1, o);
+  page_pv<D, MODE, SLAB>(rec + PB, vsc, si, gid, t4, b0, b1, o);
 }
 
+// Query words of this lane for item `item`: DK dims of query head (first head of
+// the item's group + gid), zeros for lanes past the group's head count.
 template <int D>
-__global__ void __launch_bounds__(DecodeTraits<D>::kThreads, 3)
-    decode_partials_kernel(const DecodeParams p) {
+__device__ __forceinline__ void load_query(const DecodeParams &p, int item, int gid, int t4,
+                                           uint32_t (&qw)[D / 8]) {
+  constexpr int DK = D / 4;
+  const int ipb = p.kv_heads * p.qgroups;
+  const int b = item / ipb, r = item - b * ipb;
+  const int kvh = r / p.qgroups, qg = r - kvh * p.qgroups;
+  const int nq = min(8, p.gqa - 8 * qg);
+  if (gid < nq) {
+    const __half *qp = p.q + (int64_t)b * p.q_bs + (int64_t)(kvh * p.gqa + 8 * qg + gid) * p.q_hs + t4 * DK;
+#pragma unroll
+    for (int i = 0; i < DK / 8; ++i) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4 *>(qp) + i);
+      qw[4 * i] = v.x, qw[4 * i + 1] = v.y, qw[4 * i + 2] = v.z, qw[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < DK / 2; ++i) qw[i] = 0u;
+  }
+}
+
+// B fragments of Q.K^T from the query words, permuted like the K fragments.
+template <int D>
+__device__ __forceinline__ void query_fragments(const uint32_t (&qw)[D / 8], uint32_t (&qf)[D / 16][2]) {
+#pragma unroll
+  for (int c = 0; c < D / 16; ++c) {
+    const int j = c >> 1, hb = c & 1;
+    qf[c][0] = prmt(qw[4 * j + hb], qw[4 * j + 2 + hb], 0x5410);
+    qf[c][1] = prmt(qw[4 * j + hb], qw[4 * j + 2 + hb], 0x7632);
+  }
+}
+
+// SLAB: one scale per 16-token slab (group = 16 * head_dim), the
+// per-block-per-KV-head layout; false: per-row groups (32/64/128).
+template <int D, bool SLAB>
+__global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kCtasPerSm)
+    decode_streamk_kernel(const DecodeParams p) {
   using T = DecodeTraits<D>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, t4 = lane & 3;
-  const int split = blockIdx.x;
-  const int kvh = blockIdx.y / p.qgroups, qg = blockIdx.y % p.qgroups;
-  const int b = blockIdx.z;
-  const int q0 = kvh * p.gqa + qg * 8;
-  const int nq = min(8, p.gqa - qg * 8);
-  const int nblk = p.seq_blocks ? min(p.seq_blocks[b], p.max_blocks) : p.max_blocks;
-  const int lo = split * p.chunk, hi = min(lo + p.chunk, nblk);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    int32_t *h = p.header;
+    h[kMagic] = kHeaderMagic, h[kWarpsF] = p.warps, h[kSmaxF] = p.smax, h[kRangeF] = p.range;
+    h[kMaxBlocksF] = p.max_blocks, h[kItemsF] = p.items, h[kKvHeadsF] = p.kv_heads;
+    h[kQGroupsF] = p.qgroups, h[kGqaF] = p.gqa, h[kHeadDimF] = D, h[kSlotHeadsF] = p.slot_heads;
+    h[kQHeadsF] = p.q_heads, h[kBatchF] = p.batch;
+  }
+  const int gw = blockIdx.x * T::kWarps + warp;
+  const int mb = p.max_blocks;
+  const int total = p.items * mb;
+  const int e_begin = gw * p.range;
+  const int e_end = min(e_begin + p.range, total);
+  if (gw >= p.warps || e_begin >= e_end) return;  // whole warps only; no CTA-wide barriers below
+  const int first_item = e_begin / mb, last_seg = (e_end - 1) / mb - first_item;
+  const int ipb = p.kv_heads * p.qgroups;
 
   uint8_t *ring = smem + warp * T::kRing;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + T::kWarps * T::kRing) + warp * T::kSlots;
@@ -291,28 +383,6 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, 3)
                                                       T::kWarps * T::kSlots * 8) + warp * T::kSlots;
   uint32_t *slot_meta = slot_start + T::kWarps * T::kSlots;
 
-  // Query fragments (B operand of Q.K^T), permuted like the K fragments.
-  uint32_t qf[T::kTiles][2];
-  {
-    uint32_t qw[T::DK / 2];
-    if (gid < nq) {
-      const __half *qp = p.q + (int64_t)b * p.q_bs + (int64_t)(q0 + gid) * p.q_hs + t4 * T::DK;
-#pragma unroll
-      for (int i = 0; i < T::DK / 8; ++i) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(qp) + i);
-        qw[4 * i] = v.x, qw[4 * i + 1] = v.y, qw[4 * i + 2] = v.z, qw[4 * i + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < T::DK / 2; ++i) qw[i] = 0u;
-    }
-#pragma unroll
-    for (int c = 0; c < T::kTiles; ++c) {
-      const int j = c >> 1, hb = c & 1;
-      qf[c][0] = prmt(qw[4 * j + hb], qw[4 * j + 2 + hb], 0x5410);
-      qf[c][1] = prmt(qw[4 * j + hb], qw[4 * j + 2 + hb], 0x7632);
-    }
-  }
   const int lg = p.log2_group;
   ScaleIdx si;
   si.k0 = (gid * D + t4 * T::DK) >> lg;
@@ -321,6 +391,10 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, 3)
   si.vb = ((2 * t4 + 1) * D + gid * T::DV) >> lg;
   si.vc = ((2 * t4 + 8) * D + gid * T::DV) >> lg;
   si.vd = ((2 * t4 + 9) * D + gid * T::DV) >> lg;
+  const uint32_t scale_bytes = 2u * (uint32_t)((kBlock * D) >> lg);
+  const uint32_t rb4 = (2u * (uint32_t)payload_bytes(D, AKV_MODE_INT4) + 2u * scale_bytes + 15u) & ~15u;
+  const uint32_t rb8 = (2u * (uint32_t)payload_bytes(D, AKV_MODE_INT8) + 2u * scale_bytes + 15u) & ~15u;
+  constexpr uint32_t rb16 = 2u * kBlock * D * 2u;
 
   if (lane == 0) {
 #pragma unroll
@@ -329,52 +403,146 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, 3)
   }
   __syncwarp();
 
-  float o[T::kTiles][4];
-#pragma unroll
-  for (int m = 0; m < T::kTiles; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.f;
-  SoftmaxState st{-INFINITY, -INFINITY, 0.f, 0.f};
+  // ---- page windows: 32 consecutive flattened indices, one per lane.  The
+  //      descriptor loads of the next window are issued a window ahead; when a
+  //      window becomes current every lane turns its descriptor into a ready
+  //      record (source offset, bytes, slot meta) and a ballot marks the pages
+  //      to copy, so issuing a page is a find-first-set and three shuffles.
+  auto fetch = [&](int w0, int64_t &raw, int &nb) {
+    const int e = w0 + lane;
+    raw = 0;
+    nb = 0;
+    if (e < e_end) {
+      const int it = e / mb, bb = it / ipb;
+      nb = p.seq_blocks ? min(__ldg(p.seq_blocks + bb), mb) : mb;
+      raw = __ldg(p.table + (int64_t)bb * p.table_stride + (e - it * mb));
+    }
+  };
+  int64_t w_src = 0;
+  uint32_t w_rb = 0, w_meta = 0, w_mask = 0;
+  auto prepare = [&](int w0, int64_t raw, int nb) {
+    const int e = w0 + lane;
+    bool ok = false;
+    if (e < e_end) {
+      const int it = e / mb, j = e - it * mb;
+      const int mode = j < nb ? desc_mode(raw) : AKV_MODE_SKIP;
+      w_rb = mode == AKV_MODE_FP16 ? rb16 : (mode == AKV_MODE_INT8 ? rb8 : rb4);
+      const int64_t poff = desc_offset(raw);
+      ok = mode != AKV_MODE_SKIP;
+      if (ok && ((poff & 15) || poff + (int64_t)p.kv_heads * w_rb > p.arena_bytes)) {
+        set_status(p.status, AKV_DEV_BAD_DESCRIPTOR);
+        ok = false;
+      }
+      w_src = poff + (int64_t)((it % ipb) / p.qgroups) * w_rb;
+      w_meta = (uint32_t)mode | ((uint32_t)desc_ntok(raw) << 4) | ((uint32_t)(it - first_item) << 16);
+    }
+    w_mask = __ballot_sync(0xffffffffu, ok);
+  };
+  int win0 = e_begin;
+  int64_t nxt_raw;
+  int nxt_nb;
+  {
+    int64_t raw;
+    int nb;
+    fetch(win0, raw, nb);
+    fetch(win0 + 32, nxt_raw, nxt_nb);
+    prepare(win0, raw, nb);
+  }
 
-  const int64_t *trow = p.table + (int64_t)b * p.table_stride;
-  const int64_t scale_bytes = (int64_t)2 * ((kBlock * D) >> lg);
-  int pj = lo + warp;
   uint32_t head = 0, tail = 0;  // virtual byte counters of the ring
   int issued = 0, consumed = 0;
   bool timed_out = false;
 
+  uint32_t qf[T::kTiles][2];
+  {
+    uint32_t qw[D / 8];
+    load_query<D>(p, first_item, gid, t4, qw);
+    query_fragments<D>(qw, qf);
+  }
+  float o[T::kTiles][4];
+#pragma unroll
+  for (int m = 0; m < T::kTiles; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.f;
+  SoftmaxState st{-INFINITY, -INFINITY, 0.f, 0.f};
+  int cur_seg = 0;
+
+  auto finalize = [&](int seg) {
+    float l0 = st.l0, l1 = st.l1;
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    const int item = first_item + seg;
+    const int qg = (item % ipb) % p.qgroups;
+    const int nq = min(8, p.gqa - 8 * qg);
+    float *base = p.partials + ((int64_t)gw * p.smax + seg) * p.slot_heads * (D + 2);
+    // Scalar stores: the accumulators stay in the MMA's register quads (a
+    // float2 pairing of (c0, c2) would fight that allocation on every page).
+    const int h0 = 2 * t4, h1 = 2 * t4 + 1;
+    if (h0 < nq) {
+      float *row = base + h0 * (D + 2) + T::DV * gid;
+#pragma unroll
+      for (int m = 0; m < T::kTiles; ++m) row[2 * m] = o[m][0], row[2 * m + 1] = o[m][2];
+      if (gid == 0) base[h0 * (D + 2) + D] = st.m0, base[h0 * (D + 2) + D + 1] = l0;
+    }
+    if (h1 < nq) {
+      float *row = base + h1 * (D + 2) + T::DV * gid;
+#pragma unroll
+      for (int m = 0; m < T::kTiles; ++m) row[2 * m] = o[m][1], row[2 * m + 1] = o[m][3];
+      if (gid == 0) base[h1 * (D + 2) + D] = st.m1, base[h1 * (D + 2) + D + 1] = l1;
+    }
+  };
+  auto next_segment = [&]() {
+    ++cur_seg;
+#pragma unroll
+    for (int m = 0; m < T::kTiles; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.f;
+    st = SoftmaxState{-INFINITY, -INFINITY, 0.f, 0.f};
+    if (cur_seg <= last_seg) {  // each warp meets only a few items: load the next query directly
+      uint32_t qw[D / 8];
+      load_query<D>(p, first_item + cur_seg, gid, t4, qw);
+      query_fragments<D>(qw, qf);
+    }
+  };
+
   while (true) {
     // Producer: keep up to kSlots records in flight while the ring has room.
-    while (issued - consumed < T::kSlots && pj < hi) {
-      const int64_t d = __ldg(trow + pj);
-      const int mode = desc_mode(d);
-      if (mode == AKV_MODE_SKIP) {
-        pj += T::kWarps;
+    while (issued - consumed < T::kSlots) {
+      if (w_mask == 0) {
+        if (win0 + 32 >= e_end) break;  // no pages left
+        win0 += 32;
+        const int64_t raw = nxt_raw;
+        const int nb = nxt_nb;
+        fetch(win0 + 32, nxt_raw, nxt_nb);
+        prepare(win0, raw, nb);
         continue;
       }
-      const int64_t pb = payload_bytes(D, mode);
-      const uint32_t rb =
-          (uint32_t)((2 * pb + (mode == AKV_MODE_FP16 ? 0 : 2 * scale_bytes) + 15) & ~(int64_t)15);
-      const int64_t poff = desc_offset(d);
-      if ((poff & 15) || poff < 0 || poff + (int64_t)p.kv_heads * rb > p.arena_bytes) {
-        if (lane == 0) set_status(p.status, AKV_DEV_BAD_DESCRIPTOR);
-        pj += T::kWarps;
-        continue;
-      }
+      const int k = __ffs(w_mask) - 1;
+      const uint32_t rb = __shfl_sync(0xffffffffu, w_rb, k);
+      // Virtual byte counters grow monotonically (a warp moves far less than
+      // 4 GB per launch); the physical offset is mod kRing.
       uint32_t start = head;
-      const uint32_t phys = start & (T::kRing - 1);
-      if (phys + rb > (uint32_t)T::kRing) start += T::kRing - phys;  // wrap to the next lap
-      if (start + rb - tail > (uint32_t)T::kRing) break;              // wait for room
+      const uint32_t phys = start % (uint32_t)T::kRing;
+      if (issued == consumed && phys != 0) {  // empty ring: restart at a lap boundary
+        start += T::kRing - phys;
+        tail = start;
+      } else if (phys + rb > (uint32_t)T::kRing) {
+        start += T::kRing - phys;  // wrap to the next lap
+      }
+      if (start + rb - tail > (uint32_t)T::kRing) break;  // wait for room
+      const int64_t src = __shfl_sync(0xffffffffu, w_src, k);
+      const uint32_t meta = __shfl_sync(0xffffffffu, w_meta, k);
       const int slot = issued % T::kSlots;
       if (lane == 0) {
         slot_start[slot] = start;
-        slot_meta[slot] = (uint32_t)mode | ((uint32_t)desc_ntok(d) << 8);
+        slot_meta[slot] = meta;
         fence_proxy_async_smem();  // prior generic reads of this space before the async write
         const uint32_t bar = smem_u32(&bars[slot]);
         mbar_expect_tx(bar, rb);
-        bulk_g2s(smem_u32(ring + (start & (T::kRing - 1))), p.arena + poff + (int64_t)kvh * rb, rb, bar);
+        bulk_g2s(smem_u32(ring + start % (uint32_t)T::kRing), p.arena + src, rb, bar);
       }
       head = start + rb;
       ++issued;
-      pj += T::kWarps;
+      w_mask &= w_mask - 1;
     }
     __syncwarp();
     if (issued == consumed) break;
@@ -385,17 +553,22 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, 3)
       break;
     }
     const uint32_t meta = slot_meta[slot];
-    uint8_t *rec = ring + (slot_start[slot] & (T::kRing - 1));
-    const int ntok = (int)(meta >> 8);
+    uint8_t *rec = ring + slot_start[slot] % (uint32_t)T::kRing;
+    const int seg = (int)(meta >> 16);
+    while (cur_seg < seg) {
+      finalize(cur_seg);
+      next_segment();
+    }
+    const int ntok = (int)((meta >> 4) & 31);
     switch (meta & 3u) {
       case AKV_MODE_INT4:
-        page_attend<D, AKV_MODE_INT4>(rec, ntok, lane, lg, si, qf, p.scale_log2, st, o);
+        page_attend<D, AKV_MODE_INT4, SLAB>(rec, ntok, lane, lg, si, qf, p.scale_log2, st, o);
         break;
       case AKV_MODE_INT8:
-        page_attend<D, AKV_MODE_INT8>(rec, ntok, lane, lg, si, qf, p.scale_log2, st, o);
+        page_attend<D, AKV_MODE_INT8, SLAB>(rec, ntok, lane, lg, si, qf, p.scale_log2, st, o);
         break;
       default:
-        page_attend<D, AKV_MODE_FP16>(rec, ntok, lane, lg, si, qf, p.scale_log2, st, o);
+        page_attend<D, AKV_MODE_FP16, SLAB>(rec, ntok, lane, lg, si, qf, p.scale_log2, st, o);
         break;
     }
     __syncwarp();
@@ -404,90 +577,143 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, 3)
   }
   if (timed_out) {
     if (lane == 0) set_status(p.status, AKV_DEV_TIMEOUT);
-    // Let the copies still in flight land (bounded) before the CTA exits.
+    // Let the copies still in flight land (bounded) before the warp exits.
     for (int k = consumed; k < issued; ++k)
       if (!mbar_wait_bounded(smem_u32(&bars[k % T::kSlots]), (uint32_t)(k / T::kSlots) & 1u)) break;
   }
-
-  // ---- merge the 4 warps in shared memory, write one partial per query head
-#pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    st.l0 += __shfl_xor_sync(0xffffffffu, st.l0, off);
-    st.l1 += __shfl_xor_sync(0xffffffffu, st.l1, off);
-  }
-  __syncthreads();
-  constexpr int RS = D + 2;
-  float *red = reinterpret_cast<float *>(smem);
-  float *mine = red + warp * 8 * RS;
-  const int h0 = 2 * t4, h1 = 2 * t4 + 1;
-#pragma unroll
-  for (int m = 0; m < T::kTiles; ++m) {
-    const int dd = T::DV * gid + 2 * m;
-    mine[h0 * RS + dd] = o[m][0];
-    mine[h1 * RS + dd] = o[m][1];
-    mine[h0 * RS + dd + 1] = o[m][2];
-    mine[h1 * RS + dd + 1] = o[m][3];
-  }
-  if (gid == 0) {
-    mine[h0 * RS + D] = st.m0, mine[h0 * RS + D + 1] = st.l0;
-    mine[h1 * RS + D] = st.m1, mine[h1 * RS + D + 1] = st.l1;
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < nq * D; idx += T::kThreads) {
-    const int n = idx / D, dd = idx % D;
-    float mw[T::kWarps], top = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < T::kWarps; ++w) {
-      mw[w] = red[(w * 8 + n) * RS + D];
-      top = fmaxf(top, mw[w]);
-    }
-    float acc = 0.f, den = 0.f;
-#pragma unroll
-    for (int w = 0; w < T::kWarps; ++w) {
-      const float e = mw[w] == -INFINITY ? 0.f : ex2(mw[w] - top);
-      acc += e * red[(w * 8 + n) * RS + dd];
-      den += e * red[(w * 8 + n) * RS + D + 1];
-    }
-    float *out = p.partials + (((int64_t)b * p.q_heads + q0 + n) * p.splits + split) * RS;
-    out[dd] = acc;
-    if (dd == 0) out[D] = top, out[D + 1] = den;
+  // Items past the last record (or with no visible page) still get a partial.
+  while (true) {
+    finalize(cur_seg);
+    if (cur_seg >= last_seg) break;
+    next_segment();
   }
 }
 
-// One CTA of head_dim threads per (query head, sequence).
+// Merge the partial states of the warps that touched each (sequence, query
+// head).  One CTA of head_dim threads per (query head, sequence).
 template <int D>
-__global__ void __launch_bounds__(D) merge_kernel(const float *__restrict__ partials, int q_heads,
-                                                  int splits, __half *__restrict__ out, int64_t obs,
-                                                  int64_t ohs, float *__restrict__ state) {
+__global__ void __launch_bounds__(D) merge_kernel(const int32_t *__restrict__ header,
+                                                  const float *__restrict__ partials,
+                                                  __half *__restrict__ out, int64_t obs, int64_t ohs,
+                                                  float *__restrict__ state, int32_t *status) {
   constexpr int RS = D + 2;
+  if (header[kMagic] != kHeaderMagic || header[kHeadDimF] != D) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+    return;
+  }
+  const int warps = header[kWarpsF], smax = header[kSmaxF], range = header[kRangeF];
+  const int mb = header[kMaxBlocksF], kv_heads = header[kKvHeadsF], qgroups = header[kQGroupsF];
+  const int gqa = header[kGqaF], slot_heads = header[kSlotHeadsF];
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-  const float *base = partials + ((int64_t)b * q_heads + h) * (int64_t)splits * RS;
+  const int kvh = h / gqa, r = h - kvh * gqa, qg = r >> 3, n = r & 7;
+  const int64_t item = ((int64_t)b * kv_heads + kvh) * qgroups + qg;
+  int64_t w0 = 0, w1 = -1;
+  if (mb > 0) {
+    w0 = item * mb / range;
+    w1 = ((item + 1) * mb - 1) / range;
+    if (w1 > warps - 1) w1 = warps - 1;
+  }
   float top = -INFINITY;
-  for (int s = 0; s < splits; ++s) top = fmaxf(top, base[s * RS + D]);
+  for (int64_t w = w0; w <= w1; ++w) {
+    const int64_t seg = item - (w * range) / mb;
+    top = fmaxf(top, partials[((w * smax + seg) * slot_heads + n) * RS + D]);
+  }
   float num = 0.f, den = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    const float m = base[s * RS + D];
-    const float w = m == -INFINITY ? 0.f : ex2(m - top);  // empty split weighs 0 (triton_decode.py:78)
-    num += w * base[s * RS + d];
-    den += w * base[s * RS + D + 1];
+  for (int64_t w = w0; w <= w1; ++w) {
+    const int64_t seg = item - (w * range) / mb;
+    const float *pr = partials + ((w * smax + seg) * slot_heads + n) * RS;
+    const float m = pr[D];
+    const float wt = m == -INFINITY ? 0.f : ex2(m - top);  // empty share weighs 0 (triton_decode.py:78)
+    num += wt * pr[d];
+    den += wt * pr[D + 1];
   }
   if (out) out[(int64_t)b * obs + (int64_t)h * ohs + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
   if (state) {
-    float *st = state + ((int64_t)b * q_heads + h) * RS;
+    float *st = state + ((int64_t)b * gridDim.x + h) * RS;
     st[d] = num;
     if (d == 0) st[D] = top, st[D + 1] = den;
   }
 }
 
+// Merge n already-merged states laid out [n][batch][q_heads][D+2] (e.g. gathered
+// from n GPUs) into the normalised output.
 template <int D>
-static int launch_decode(const DecodeParams &p, int batch, cudaStream_t stream) {
+__global__ void __launch_bounds__(D) merge_states_kernel(const float *__restrict__ states, int n,
+                                                         int q_heads, int batch, __half *__restrict__ out,
+                                                         int64_t obs, int64_t ohs) {
+  constexpr int RS = D + 2;
+  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const int64_t stride = (int64_t)batch * q_heads * RS;
+  const float *base = states + ((int64_t)b * q_heads + h) * RS;
+  float top = -INFINITY;
+  for (int s = 0; s < n; ++s) top = fmaxf(top, base[s * stride + D]);
+  float num = 0.f, den = 0.f;
+  for (int s = 0; s < n; ++s) {
+    const float m = base[s * stride + D];
+    const float wt = m == -INFINITY ? 0.f : ex2(m - top);
+    num += wt * base[s * stride + d];
+    den += wt * base[s * stride + D + 1];
+  }
+  out[(int64_t)b * obs + (int64_t)h * ohs + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+}
+
+// ------------------------------------------------------------------- host
+struct Plan {
+  int warps, range, smax, slot_heads, items, qgroups, ctas;
+  int64_t bytes;
+};
+
+template <int D>
+static int device_warps(int *out) {
   using T = DecodeTraits<D>;
-  if (cudaFuncSetAttribute(decode_partials_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return AKV_ERR_CUDA;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return AKV_ERR_CUDA;
+  int per_sm_slab = 0;
+  if (cudaFuncSetAttribute(decode_streamk_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           T::kSmem) != cudaSuccess ||
+      cudaFuncSetAttribute(decode_streamk_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            T::kSmem) != cudaSuccess)
     return AKV_ERR_CUDA;
-  const dim3 grid(p.splits, p.kv_heads * p.qgroups, batch);
-  decode_partials_kernel<D><<<grid, T::kThreads, T::kSmem, stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_streamk_kernel<D, false>, T::kThreads,
+                                                    T::kSmem) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_slab, decode_streamk_kernel<D, true>,
+                                                    T::kThreads, T::kSmem) != cudaSuccess)
+    return AKV_ERR_CUDA;
+  per_sm = std::min(per_sm, per_sm_slab);  // both variants get the same decomposition
+  if (per_sm < 1) return AKV_ERR_CUDA;
+  *out = sms * per_sm * T::kWarps;
+  return AKV_OK;
+}
+
+static int make_plan(int batch, int q_heads, int kv_heads, int head_dim, int max_blocks, int splits,
+                     Plan *plan) {
+  if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || max_blocks < 0 || q_heads % kv_heads)
+    return AKV_ERR_INVALID;
+  if (head_dim != 64 && head_dim != 128) return AKV_ERR_UNSUPPORTED;
+  const int gqa = q_heads / kv_heads;
+  Plan pl;
+  pl.qgroups = (gqa + 7) / 8;
+  pl.slot_heads = std::min(8, gqa);
+  const int64_t items = (int64_t)batch * kv_heads * pl.qgroups;
+  const int64_t total = items * max_blocks;
+  if (items > (1 << 30) || total >= (1ll << 31)) return AKV_ERR_UNSUPPORTED;
+  pl.items = (int)items;
+  int dev_warps = 0;
+  const int st = head_dim == 64 ? device_warps<64>(&dev_warps) : device_warps<128>(&dev_warps);
+  if (st != AKV_OK) return st;
+  int64_t warps = dev_warps;
+  if (splits > 0) warps = std::min<int64_t>(warps, items * (int64_t)splits);
+  warps = std::max<int64_t>(1, std::min<int64_t>(warps, std::max<int64_t>(total, 1)));
+  const int64_t range = std::max<int64_t>(1, (total + warps - 1) / warps);
+  warps = std::max<int64_t>(1, (total + range - 1) / range);
+  pl.range = (int)range;
+  pl.warps = (int)warps;
+  pl.smax = max_blocks > 0 ? (int)(1 + (range - 1 + max_blocks - 1) / max_blocks) : 1;
+  pl.ctas = (int)((warps + DecodeTraits<128>::kWarps - 1) / DecodeTraits<128>::kWarps);
+  pl.bytes = kHeaderBytes + (int64_t)pl.warps * pl.smax * pl.slot_heads * (head_dim + 2) * 4;
+  *plan = pl;
+  return AKV_OK;
 }
 
 static int ilog2_exact(int x) {
@@ -500,9 +726,11 @@ static int ilog2_exact(int x) {
 
 using namespace akv;
 
-extern "C" int64_t akv_workspace_bytes(int batch, int q_heads, int splits, int head_dim) {
-  if (batch <= 0 || q_heads <= 0 || splits <= 0 || head_dim <= 0) return 0;
-  return (int64_t)batch * q_heads * splits * (head_dim + 2) * (int64_t)sizeof(float);
+extern "C" int64_t akv_workspace_bytes(int batch, int q_heads, int kv_heads, int head_dim,
+                                       int max_blocks, int splits) {
+  Plan pl;
+  if (make_plan(batch, q_heads, kv_heads, head_dim, max_blocks, splits, &pl) != AKV_OK) return -1;
+  return pl.bytes;
 }
 
 extern "C" int akv_decode_partials(const void *arena, int64_t arena_bytes, const int64_t *table,
@@ -510,18 +738,18 @@ extern "C" int akv_decode_partials(const void *arena, int64_t arena_bytes, const
                                    int32_t max_blocks, const void *query, int64_t q_batch_stride,
                                    int64_t q_head_stride, int32_t batch, int32_t q_heads,
                                    int32_t kv_heads, int32_t head_dim, int32_t group, float scale,
-                                   int32_t splits, float *partials, int32_t *dev_status,
-                                   void *stream) {
-  if (!arena || !table || !query || !partials) return AKV_ERR_INVALID;
-  if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || splits <= 0 || max_blocks < 0) return AKV_ERR_INVALID;
-  if (q_heads % kv_heads) return AKV_ERR_INVALID;
+                                   int32_t splits, void *workspace, int64_t workspace_bytes,
+                                   int32_t *dev_status, void *stream) {
+  if (!arena || !table || !query || !workspace) return AKV_ERR_INVALID;
   if (table_stride < max_blocks || arena_bytes < 0 || !isfinite(scale)) return AKV_ERR_INVALID;
-  if (head_dim != 64 && head_dim != 128) return AKV_ERR_UNSUPPORTED;
+  if (((uintptr_t)arena & 15) || ((uintptr_t)query & 15) || ((uintptr_t)workspace & 15))
+    return AKV_ERR_INVALID;
+  if (q_batch_stride % 8 || q_head_stride % 8) return AKV_ERR_INVALID;
   const int lg = ilog2_exact(group);
   if (lg < 0 || group < head_dim / 4 || group > 16 * head_dim) return AKV_ERR_UNSUPPORTED;
-  if (((uintptr_t)arena & 15) || ((uintptr_t)query & 15)) return AKV_ERR_INVALID;
-  if (q_batch_stride % 8 || q_head_stride % 8) return AKV_ERR_INVALID;
-  if (batch > 65535 || (int64_t)kv_heads * ((q_heads / kv_heads + 7) / 8) > 65535) return AKV_ERR_UNSUPPORTED;
+  Plan pl;
+  if (int st = make_plan(batch, q_heads, kv_heads, head_dim, max_blocks, splits, &pl)) return st;
+  if (workspace_bytes < pl.bytes) return AKV_ERR_INVALID;
   DecodeParams p;
   p.arena = (const uint8_t *)arena;
   p.arena_bytes = arena_bytes;
@@ -532,34 +760,65 @@ extern "C" int akv_decode_partials(const void *arena, int64_t arena_bytes, const
   p.q = (const __half *)query;
   p.q_bs = q_batch_stride;
   p.q_hs = q_head_stride;
+  p.batch = batch;
   p.q_heads = q_heads;
   p.kv_heads = kv_heads;
   p.gqa = q_heads / kv_heads;
-  p.qgroups = (p.gqa + 7) / 8;
-  p.splits = splits;
-  p.chunk = (max_blocks + splits - 1) / splits;
+  p.qgroups = pl.qgroups;
+  p.items = pl.items;
   p.log2_group = lg;
+  p.warps = pl.warps;
+  p.range = pl.range;
+  p.smax = pl.smax;
+  p.slot_heads = pl.slot_heads;
   p.scale_log2 = scale * 1.4426950408889634f;  // scores in base 2: exp(x) = 2^(x log2 e)
-  p.partials = partials;
+  p.header = (int32_t *)workspace;
+  p.partials = (float *)((uint8_t *)workspace + kHeaderBytes);
   p.status = dev_status;
   cudaStream_t s = (cudaStream_t)stream;
-  return head_dim == 64 ? launch_decode<64>(p, batch, s) : launch_decode<128>(p, batch, s);
+  const bool slab = group == 16 * head_dim;
+  if (head_dim == 64) {
+    if (slab) decode_streamk_kernel<64, true><<<pl.ctas, DecodeTraits<64>::kThreads, DecodeTraits<64>::kSmem, s>>>(p);
+    else decode_streamk_kernel<64, false><<<pl.ctas, DecodeTraits<64>::kThreads, DecodeTraits<64>::kSmem, s>>>(p);
+  } else {
+    if (slab) decode_streamk_kernel<128, true><<<pl.ctas, DecodeTraits<128>::kThreads, DecodeTraits<128>::kSmem, s>>>(p);
+    else decode_streamk_kernel<128, false><<<pl.ctas, DecodeTraits<128>::kThreads, DecodeTraits<128>::kSmem, s>>>(p);
+  }
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
 }
 
-extern "C" int akv_merge(const float *partials, int32_t batch, int32_t q_heads, int32_t splits,
-                         int32_t head_dim, void *out, int64_t out_batch_stride,
-                         int64_t out_head_stride, float *state_out, void *stream) {
-  if (!partials || (!out && !state_out)) return AKV_ERR_INVALID;
-  if (batch <= 0 || q_heads <= 0 || splits <= 0 || batch > 65535) return AKV_ERR_INVALID;
+extern "C" int akv_merge(const void *workspace, int32_t batch, int32_t q_heads, int32_t head_dim,
+                         void *out, int64_t out_batch_stride, int64_t out_head_stride,
+                         float *state_out, int32_t *dev_status, void *stream) {
+  if (!workspace || (!out && !state_out)) return AKV_ERR_INVALID;
+  if (batch <= 0 || q_heads <= 0 || batch > 65535) return AKV_ERR_INVALID;
+  if (head_dim != 64 && head_dim != 128) return AKV_ERR_UNSUPPORTED;
+  const int32_t *header = (const int32_t *)workspace;
+  const float *partials = (const float *)((const uint8_t *)workspace + kHeaderBytes);
+  const dim3 grid(q_heads, batch);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (head_dim == 64)
+    merge_kernel<64><<<grid, 64, 0, s>>>(header, partials, (__half *)out, out_batch_stride,
+                                         out_head_stride, state_out, dev_status);
+  else
+    merge_kernel<128><<<grid, 128, 0, s>>>(header, partials, (__half *)out, out_batch_stride,
+                                           out_head_stride, state_out, dev_status);
+  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+}
+
+extern "C" int akv_merge_states(const float *states, int32_t n, int32_t batch, int32_t q_heads,
+                                int32_t head_dim, void *out, int64_t out_batch_stride,
+                                int64_t out_head_stride, void *stream) {
+  if (!states || !out || n <= 0 || batch <= 0 || q_heads <= 0 || batch > 65535) return AKV_ERR_INVALID;
   if (head_dim != 64 && head_dim != 128) return AKV_ERR_UNSUPPORTED;
   const dim3 grid(q_heads, batch);
   cudaStream_t s = (cudaStream_t)stream;
   if (head_dim == 64)
-    merge_kernel<64><<<grid, 64, 0, s>>>(partials, q_heads, splits, (__half *)out, out_batch_stride,
-                                         out_head_stride, state_out);
+    merge_states_kernel<64><<<grid, 64, 0, s>>>(states, n, q_heads, batch, (__half *)out,
+                                                out_batch_stride, out_head_stride);
   else
-    merge_kernel<128><<<grid, 128, 0, s>>>(partials, q_heads, splits, (__half *)out,
-                                           out_batch_stride, out_head_stride, state_out);
+    merge_states_kernel<128><<<grid, 128, 0, s>>>(states, n, q_heads, batch, (__half *)out,
+                                                  out_batch_stride, out_head_stride);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
 }
 
@@ -571,19 +830,18 @@ extern "C" int akv_packed_attention(const void *arena, int64_t arena_bytes, cons
                                     int32_t splits, void *out, int64_t out_batch_stride,
                                     int64_t out_head_stride, void *workspace,
                                     int64_t workspace_bytes, int32_t *dev_status, void *stream) {
-  if (!out || !workspace) return AKV_ERR_INVALID;
-  if (workspace_bytes < akv_workspace_bytes(batch, q_heads, splits, head_dim)) return AKV_ERR_INVALID;
+  if (!out) return AKV_ERR_INVALID;
   int st = akv_decode_partials(arena, arena_bytes, table, table_stride, seq_blocks, max_blocks, query,
                                q_batch_stride, q_head_stride, batch, q_heads, kv_heads, head_dim,
-                               group, scale, splits, (float *)workspace, dev_status, stream);
+                               group, scale, splits, workspace, workspace_bytes, dev_status, stream);
   if (st != AKV_OK) return st;
-  return akv_merge((const float *)workspace, batch, q_heads, splits, head_dim, out, out_batch_stride,
-                   out_head_stride, nullptr, stream);
+  return akv_merge(workspace, batch, q_heads, head_dim, out, out_batch_stride, out_head_stride,
+                   nullptr, dev_status, stream);
 }
 
 // ===================================================== allocation-free variant
-// akv_packed_attention_static: the same decode + merge, with the split-K
-// partials in a fixed array compiled into this library instead of a workspace
+// akv_packed_attention_static: the same decode + merge, with the partial
+// states in a fixed array compiled into this library instead of a workspace
 // the caller allocates.  For callers that cannot allocate device memory: hosts
 // that reserve all of HBM up front for their own pool (a serving engine's KV
 // pool), latency-critical decode loops where cudaMalloc/cudaFree would
@@ -591,15 +849,13 @@ extern "C" int akv_packed_attention(const void *arena, int64_t arena_bytes, cons
 //
 // Every GPU that loads the library holds the array (kStaticScratchBytes) until
 // the process exits.  All calls on a device share it and it keeps the last
-// call's contents: each call rewrites every partial it reads before reading
-// it, so nothing needs clearing, but calls whose kernels overlap on the GPU
-// (different streams without ordering between them) race on it.
+// call's contents: each call rewrites every partial it reads (and the header)
+// before reading it, so nothing needs clearing, but calls whose kernels overlap
+// on the GPU (different streams without ordering between them) race on it.
 namespace akv {
 constexpr int64_t kStaticScratchBytes = 8ll << 20;  // 8 MiB per GPU
 static __device__ __align__(256) float g_static_partials[kStaticScratchBytes / sizeof(float)];
 }  // namespace akv
-
-#include <mutex>
 
 namespace {
 std::mutex g_static_mu;
@@ -616,7 +872,7 @@ extern "C" int akv_packed_attention_static(const void *arena, int64_t arena_byte
                                            int32_t splits, void *out, int64_t out_batch_stride,
                                            int64_t out_head_stride, int32_t *dev_status, void *stream) {
   if (!out) return AKV_ERR_INVALID;
-  const int64_t need = akv_workspace_bytes(batch, q_heads, splits, head_dim);
+  const int64_t need = akv_workspace_bytes(batch, q_heads, kv_heads, head_dim, max_blocks, splits);
   if (need <= 0) return AKV_ERR_INVALID;
   if (need > akv::kStaticScratchBytes) return AKV_ERR_SCRATCH;
   int dev = 0;

@@ -112,37 +112,52 @@ int akv_unpack_pages(const int64_t *desc, int64_t n_pages, const void *arena,
                      int64_t arena_bytes, int heads, int head_dim, int group, void *out_k,
                      void *out_v, int32_t *dev_status, void *stream);
 
-/* Workspace bytes akv_packed_attention needs. */
-int64_t akv_workspace_bytes(int batch, int q_heads, int splits, int head_dim);
+/* Bytes of the workspace akv_decode_partials / akv_packed_attention need for
+ * this geometry on the current device (-1 for invalid or unsupported arguments).
+ * The workspace holds a 256-byte header describing the work decomposition and
+ * one partial state (acc[head_dim], m, l) per (warp, item it touched, query
+ * head); it is opaque to the caller. */
+int64_t akv_workspace_bytes(int batch, int q_heads, int kv_heads, int head_dim, int max_blocks,
+                            int splits);
 
-/* Split-K paged decode attention: one query token per sequence over mixed
- * FP16/INT8/INT4 pages.
+/* Paged decode attention, first stage: one query token per sequence over mixed
+ * FP16/INT8/INT4 pages, partial states into the workspace.
  *   table: descriptors, sequence b's pages at table[b*table_stride + j], j < blocks(b);
  *   seq_blocks: per-sequence page count (NULL: every sequence has max_blocks);
  *   query: fp16 [batch][q_heads][head_dim] with the given strides (elements);
  *   q head h attends KV head h / (q_heads / kv_heads);
- *   partials: fp32 [batch][q_heads][splits][head_dim + 2] = (acc[head_dim], m, l),
- *   m in base-2 units of the scaled score, acc and l relative to 2^m.
+ *   splits: pieces each (sequence, KV head) is cut into at most (<= 0: as many
+ *   as the device has resident warps); the kernel is persistent and gives
+ *   every warp one contiguous range of (sequence, KV head, page) work.
  * Replaces triton_decode._decode_parts (triton_decode.py:35-67). */
 int akv_decode_partials(const void *arena, int64_t arena_bytes, const int64_t *table,
                         int64_t table_stride, const int32_t *seq_blocks, int32_t max_blocks,
                         const void *query, int64_t q_batch_stride, int64_t q_head_stride,
                         int32_t batch, int32_t q_heads, int32_t kv_heads, int32_t head_dim,
-                        int32_t group, float scale, int32_t splits, float *partials,
-                        int32_t *dev_status, void *stream);
+                        int32_t group, float scale, int32_t splits, void *workspace,
+                        int64_t workspace_bytes, int32_t *dev_status, void *stream);
 
-/* Log-sum-exp merge of `splits` partial states per (sequence, query head).
- * out (nullable): fp16 [batch][q_heads][head_dim] with strides (elements);
- * state_out (nullable): fp32 [batch][q_heads][head_dim + 2] merged (acc, m, l)
- * for a further merge (e.g. across GPUs).  Empty splits weigh 0; a query with
- * no visible token gets zeros.
+/* Second stage: log-sum-exp merge of the workspace's partial states per
+ * (sequence, query head).  out (nullable): fp16 [batch][q_heads][head_dim] with
+ * strides (elements); state_out (nullable): fp32 [batch][q_heads][head_dim + 2]
+ * merged (acc, m, l), m in base-2 units of the scaled score and acc, l relative
+ * to 2^m, for a further merge (e.g. across GPUs).  Empty shares weigh 0; a
+ * query with no visible token gets zeros.
  * Replaces triton_decode._merge_parts (triton_decode.py:70-82). */
-int akv_merge(const float *partials, int32_t batch, int32_t q_heads, int32_t splits,
-              int32_t head_dim, void *out, int64_t out_batch_stride, int64_t out_head_stride,
-              float *state_out, void *stream);
+int akv_merge(const void *workspace, int32_t batch, int32_t q_heads, int32_t head_dim, void *out,
+              int64_t out_batch_stride, int64_t out_head_stride, float *state_out,
+              int32_t *dev_status, void *stream);
+
+/* Merge n states fp32 [n][batch][q_heads][head_dim + 2] (as akv_merge's
+ * state_out writes them, e.g. gathered from n GPUs holding contiguous shards of
+ * each sequence) into the fp16 output [batch][q_heads][head_dim].  The same LSE
+ * algebra as triton_decode._merge_parts (triton_decode.py:70-82). */
+int akv_merge_states(const float *states, int32_t n, int32_t batch, int32_t q_heads,
+                     int32_t head_dim, void *out, int64_t out_batch_stride,
+                     int64_t out_head_stride, void *stream);
 
 /* akv_decode_partials followed by akv_merge, partials in the caller's workspace
- * (at least akv_workspace_bytes bytes).
+ * (at least akv_workspace_bytes bytes, 16-byte aligned).
  * Replaces triton_decode.packed_attention (triton_decode.py:85-104). */
 int akv_packed_attention(const void *arena, int64_t arena_bytes, const int64_t *table,
                          int64_t table_stride, const int32_t *seq_blocks, int32_t max_blocks,
@@ -158,8 +173,8 @@ int akv_packed_attention(const void *arena, int64_t arena_bytes, const int64_t *
  * would synchronize the device, bindings holding raw pointers but no allocator.
  * The split-K partials live in a fixed array inside the library
  * (akv_static_scratch_bytes() = 8 MiB per GPU, held until process exit), so it
- * allocates nothing; requests needing more than that
- * (batch * q_heads * splits * (head_dim + 2) * 4 bytes) return AKV_ERR_SCRATCH.
+ * allocates nothing; requests whose akv_workspace_bytes exceed that return
+ * AKV_ERR_SCRATCH.
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before
  * any stream capture.  All calls on a device share the array and it keeps the

@@ -28,7 +28,7 @@ def test_library_exports_declared_symbol(name):
 
 def test_host_helpers_need_no_gpu():
     lib = _lib.load()
-    assert lib.akv_abi_version() == 1
+    assert lib.akv_abi_version() == 2
     assert _lib.status_string(_lib.ERR_INVALID).startswith("invalid")
     for dim in (64, 128):
         for group in (32, 64, 128, 16 * dim):
@@ -36,7 +36,6 @@ def test_host_helpers_need_no_gpu():
                 assert lib.akv_record_bytes(dim, group, mode) == P.record_bytes(dim, group, bits)
     assert lib.akv_record_bytes(128, 2048, _lib.MODE_SKIP) == 0
     assert lib.akv_record_bytes(128, 3, _lib.MODE_INT4) == -1
-    assert lib.akv_workspace_bytes(2, 16, 4, 128) == 2 * 16 * 4 * 130 * 4
 
 
 def test_invalid_arguments_are_rejected_before_any_launch():
@@ -45,6 +44,8 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     lib = _lib.load()
     assert lib.akv_quantize(None, 0, 10, 16, 8, 0, None, None, None) == _lib.ERR_INVALID
     assert lib.akv_decode_partials(None, 0, None, 0, None, 0, None, 0, 0, 1, 1, 1, 128, 64, 1.0, 1,
-                                   None, None, None) == _lib.ERR_INVALID
+                                   None, 0, None, None) == _lib.ERR_INVALID
     with pytest.raises(ValueError):
-        _lib.call("akv_merge", None, 1, 1, 1, 128, None, 0, 0, None, None)
+        _lib.call("akv_merge", None, 1, 1, 128, None, 0, 0, None, None, None)
+    with pytest.raises(ValueError):
+        _lib.call("akv_merge_states", None, 2, 1, 1, 128, None, 0, 0, None)

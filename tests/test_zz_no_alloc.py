@@ -45,7 +45,8 @@ def _args(q, store, splits):
 def _with_workspace(q, store, splits, cuda):
     lib = _lib.load()
     out = torch.empty_like(q)
-    ws = torch.empty(lib.akv_workspace_bytes(q.shape[0], q.shape[1], splits, 128), dtype=torch.uint8, device=cuda)
+    nbytes = lib.akv_workspace_bytes(q.shape[0], q.shape[1], store.pool.heads, 128, store.max_blocks, splits)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda)
     status = lib.akv_packed_attention(*_args(q, store, splits), out.data_ptr(), out.stride(0), out.stride(1),
                                       ws.data_ptr(), ws.numel(), None, _lib.stream_of(cuda))
     assert status == _lib.OK, _lib.status_string(status)
@@ -79,9 +80,16 @@ def test_static_scratch_refuses_requests_beyond_its_size(cuda):
     lib = _lib.load()
     assert lib.akv_static_scratch_bytes() == 8 << 20
     q, store = _store(cuda, 701, batch=1, q_heads=16, kv_heads=8, tokens=64, group=2048)
-    splits = (8 << 20) // (16 * 130 * 4) + 1  # one split more than the scratch holds
+    # A geometry whose partial states need more than the fixed scratch.
+    batch = 1
+    while lib.akv_workspace_bytes(batch, 64, 8, 128, 512, 0) <= 8 << 20:
+        batch *= 2
+    q = torch.zeros(batch, 64, 1, 128, dtype=torch.float16, device=cuda)
+    splits = 0
     out = torch.empty_like(q)
-    status = lib.akv_packed_attention_static(*_args(q, store, splits), out.data_ptr(), out.stride(0),
-                                             out.stride(1), None, _lib.stream_of(cuda))
-    assert status == 4  # AKV_ERR_SCRATCH
+    args = list(_args(q, store, splits))
+    args[5], args[9], args[10], args[11] = 512, batch, 64, 8  # max_blocks, batch, q_heads, kv_heads
+    status = lib.akv_packed_attention_static(*args, out.data_ptr(), out.stride(0), out.stride(1), None,
+                                             _lib.stream_of(cuda))
+    assert status == _lib.ERR_SCRATCH
     assert "8 MiB" in _lib.status_string(status)
