@@ -45,8 +45,8 @@ template <int D>
 struct DecodeTraits {
   static constexpr int kWarps = 4;     // independent streaming warps per CTA
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kCtasPerSm = 3;
-  static constexpr int kRing = 16384;  // bytes of ring per warp
+  static constexpr int kCtasPerSm = 4;   // 16 warps per SM (128 registers, 50 KB smem per CTA)
+  static constexpr int kRing = 12288;  // bytes of ring per warp
   static constexpr int kSlots = 8;     // records in flight per warp
   static constexpr int DK = D / 4;     // K dims a lane owns per row
   static constexpr int DV = D / 8;     // V dims a lane owns per row
@@ -109,9 +109,15 @@ __device__ __forceinline__ void lds_words(const uint8_t *p, uint32_t (&w)[N]) {
 
 // Scale indices a lane needs, fixed for the whole kernel (group is a power of
 // two dividing 16*D): K rows gid and gid+8 at column t4*DK, V rows 2t4, 2t4+1,
-// 2t4+8, 2t4+9 at column gid*DV.
+// 2t4+8, 2t4+9 at column gid*DV.  Two 16-bit indices per word.
 struct ScaleIdx {
-  int k0, k1, va, vb, vc, vd;
+  uint32_t k, vab, vcd;
+  __device__ __forceinline__ int k0() const { return (int)(k & 0xffff); }
+  __device__ __forceinline__ int k1() const { return (int)(k >> 16); }
+  __device__ __forceinline__ int va() const { return (int)(vab & 0xffff); }
+  __device__ __forceinline__ int vb() const { return (int)(vab >> 16); }
+  __device__ __forceinline__ int vc() const { return (int)(vcd & 0xffff); }
+  __device__ __forceinline__ int vd() const { return (int)(vcd >> 16); }
 };
 
 // ---------------------------------------------------------------- Q . K^T
@@ -137,8 +143,8 @@ __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, c
   float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   uint32_t sc0 = 0, sc1 = 0;
   if constexpr (MODE != AKV_MODE_FP16) {
-    sc0 = rep_half(ksc + (SLAB ? 0 : si.k0));
-    sc1 = SLAB ? sc0 : rep_half(ksc + si.k1);
+    sc0 = rep_half(ksc + (SLAB ? 0 : si.k0()));
+    sc1 = SLAB ? sc0 : rep_half(ksc + si.k1());
   }
   uint32_t a0w[WHOLE ? W : 1], a1w[WHOLE ? W : 1];
   if constexpr (WHOLE) {
@@ -209,8 +215,8 @@ __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, 
     if constexpr (SLAB) {
       sab = scd = rep_half(vsc);
     } else {
-      sab = pair_half(vsc + si.va, vsc + si.vb);
-      scd = pair_half(vsc + si.vc, vsc + si.vd);
+      sab = pair_half(vsc + si.va(), vsc + si.vb());
+      scd = pair_half(vsc + si.vc(), vsc + si.vd());
     }
   }
 #pragma unroll
@@ -385,12 +391,11 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
 
   const int lg = p.log2_group;
   ScaleIdx si;
-  si.k0 = (gid * D + t4 * T::DK) >> lg;
-  si.k1 = ((gid + 8) * D + t4 * T::DK) >> lg;
-  si.va = ((2 * t4) * D + gid * T::DV) >> lg;
-  si.vb = ((2 * t4 + 1) * D + gid * T::DV) >> lg;
-  si.vc = ((2 * t4 + 8) * D + gid * T::DV) >> lg;
-  si.vd = ((2 * t4 + 9) * D + gid * T::DV) >> lg;
+  si.k = (uint32_t)((gid * D + t4 * T::DK) >> lg) | ((uint32_t)(((gid + 8) * D + t4 * T::DK) >> lg) << 16);
+  si.vab = (uint32_t)(((2 * t4) * D + gid * T::DV) >> lg) |
+           ((uint32_t)(((2 * t4 + 1) * D + gid * T::DV) >> lg) << 16);
+  si.vcd = (uint32_t)(((2 * t4 + 8) * D + gid * T::DV) >> lg) |
+           ((uint32_t)(((2 * t4 + 9) * D + gid * T::DV) >> lg) << 16);
   const uint32_t scale_bytes = 2u * (uint32_t)((kBlock * D) >> lg);
   const uint32_t rb4 = (2u * (uint32_t)payload_bytes(D, AKV_MODE_INT4) + 2u * scale_bytes + 15u) & ~15u;
   const uint32_t rb8 = (2u * (uint32_t)payload_bytes(D, AKV_MODE_INT8) + 2u * scale_bytes + 15u) & ~15u;
