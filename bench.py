@@ -57,6 +57,14 @@ WORKLOADS = {
 }
 
 
+PACK = dict(
+    name="requantize/pack, 28 layers x 32 sequences x 8 KV heads x 4096 tokens x 128 dims",
+    layers=28, batch=32, kv_heads=8, tokens=4096, dim=128, group=2048,
+    mix={16: 0.20, 8: 0.30, 4: 0.50})
+# 2 layers x 8 sequences (268 MB of fp16 input, > L2): the pack profiling case.
+PACK_SMALL = dict(PACK, name="requantize/pack, 2 layers x 8 sequences (profiling case)", layers=2, batch=8)
+
+
 def hbm_peak():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -330,6 +338,162 @@ def run_ours(args, wl):
         dist.destroy_process_group()
 
 
+def pack_cpu_baseline(seconds: float):
+    """The reference codec (quantize_tensor per 16-token slab, restated in numpy)
+    timed on the host for about ``seconds``."""
+    import numpy as np
+
+    from oracle import codec as OC
+
+    rng = np.random.default_rng(5)
+    slabs = (rng.standard_normal((64, 16, 128)) * 1.0).astype(np.float16)
+    bits = rng.choice(np.array([16, 8, 4]), size=64, p=[0.2, 0.3, 0.5])
+    nbytes = 0
+    done = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds or done < 64:
+        i = done % 64
+        x = slabs[i]
+        nbytes += x.nbytes
+        if bits[i] == 16:
+            nbytes += x.astype(np.float16).nbytes
+        else:
+            payload, scales = OC.quantize_tensor(x, int(bits[i]), 2048)
+            nbytes += payload.nbytes + scales.nbytes
+        done += 1
+    dt = time.perf_counter() - t0
+    return {"gbs": nbytes / dt / 1e9, "cores": 1,
+            "sample": f"{done} 16x128 fp16 slabs through the numpy restatement of quantize_tensor, one core"}
+
+
+def run_pack(args, wl):
+    """Bulk requantize/pack of dense fp16 K/V into page records (one launch per step)."""
+    import numpy as np
+    import torch
+
+    import anchorkv_b200 as akv
+    from anchorkv_b200 import _lib
+    from anchorkv_b200 import pool as P
+
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(device)
+    L, B, H, T, D = wl["layers"], wl["batch"], wl["kv_heads"], wl["tokens"], wl["dim"]
+    nblk = T // 16
+    rng = np.random.default_rng(7)
+    keys = list(wl["mix"])
+    bits = rng.choice(np.array(keys), size=(L * B, nblk), p=[wl["mix"][k] for k in keys])
+    counts = {b: int((bits == b).sum()) for b in (16, 8, 4)}
+    pool = P.PagePool(H, D, group=wl["group"], pages=counts, device=device, shuffle_seed=11, zero=False)
+    codes = np.zeros_like(bits)
+    offsets = np.zeros(bits.shape, np.int64)
+    for b_, mode in P.BITS_TO_MODE.items():
+        where = bits == b_
+        offsets[where] = pool.alloc_many(b_, int(where.sum()))
+        codes[where] = mode
+    desc = torch.from_numpy(P.encode_array(codes, np.full(bits.shape, 16), offsets).reshape(-1)).to(device)
+    gen = torch.Generator(device=device).manual_seed(3)
+    src = []
+    for _ in range(2):  # K and V: N(0,1) with 4 outlier channels per head scaled x(+-8)
+        x = torch.empty((L * B, H, T, D), dtype=torch.float16, device=device).normal_(generator=gen)
+        ch = torch.randint(0, D, (L * B, H, 4), generator=gen, device=device)
+        sign = torch.where(torch.rand((L * B, H, 4), generator=gen, device=device) < 0.5, -8.0, 8.0)
+        fac = torch.ones((L * B, H, D), device=device).scatter_(2, ch, sign).half()
+        x.mul_(fac[:, :, None, :])
+        src.append(x)
+    k, v = src
+    status = _lib.status_word(device)
+    stream = torch.cuda.current_stream(device)
+    lib = _lib.load()
+    n_pages = L * B * nblk
+    read = 2 * k.numel() * 2
+    written = sum(counts[b] * P.algorithmic_record_bytes(D, wl["group"], b) * H for b in (16, 8, 4))
+
+    def step():
+        assert lib.akv_pack_pages(k.data_ptr(), v.data_ptr(), H * T * D, T * D, nblk, n_pages, desc.data_ptr(),
+                                  pool.arena.data_ptr(), pool.nbytes, H, D, wl["group"], _lib.SEM_TENSOR,
+                                  status.data_ptr(), stream.cuda_stream) == 0
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    gpu_id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    sampler = ClockSampler(gpu_id)
+    time.sleep(0.3)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    clocks = sampler.stop()
+    assert akv.take_device_status(device) == 0
+    ms = t0.elapsed_time(t1) / args.steps
+    peak, peak_kind = hbm_peak()
+    gbs = (read + written) / (ms * 1e-3) / 1e9
+    # e2e: one layer's K/V copied in from pinned host memory and its page records
+    # (a contiguous pool of that layer's pages) copied back, every step.
+    k_host = k[:B].cpu().pin_memory()
+    v_host = v[:B].cpu().pin_memory()
+    layer_pages = B * nblk
+    lbits = bits[:B]
+    e2e_pool = P.PagePool(H, D, group=wl["group"], pages={b: int((lbits == b).sum()) for b in (16, 8, 4)},
+                          device=device, zero=False)
+    lcodes = np.zeros_like(lbits)
+    loffs = np.zeros(lbits.shape, np.int64)
+    for b_, mode in P.BITS_TO_MODE.items():
+        where = lbits == b_
+        loffs[where] = e2e_pool.alloc_many(b_, int(where.sum()))
+        lcodes[where] = mode
+    ldesc = torch.from_numpy(P.encode_array(lcodes, np.full(lbits.shape, 16), loffs).reshape(-1)).to(device)
+    out_host = torch.empty(e2e_pool.nbytes, dtype=torch.uint8).pin_memory()
+    kd, vd = torch.empty_like(k[:B]), torch.empty_like(v[:B])
+
+    def e2e_step():
+        kd.copy_(k_host, non_blocking=True)
+        vd.copy_(v_host, non_blocking=True)
+        assert lib.akv_pack_pages(kd.data_ptr(), vd.data_ptr(), H * T * D, T * D, nblk, layer_pages,
+                                  ldesc.data_ptr(), e2e_pool.arena.data_ptr(), e2e_pool.nbytes, H, D, wl["group"],
+                                  _lib.SEM_TENSOR, status.data_ptr(), stream.cuda_stream) == 0
+        out_host.copy_(e2e_pool.arena, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(10):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1) / 10
+    layer_bytes = 2 * k_host.numel() * 2 + sum(
+        int((lbits == b).sum()) * P.algorithmic_record_bytes(D, wl["group"], b) * H for b in (16, 8, 4))
+    line = {
+        "metric": "requantize/pack GB/s (read + written bytes)", "value": round(gbs, 1), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in, int8/int4/f16 out",
+        "data": "synthetic (seeded fp16 N(0,1), 4 outlier channels per head x(+-8))",
+        "config": {"workload": wl["name"], "precision_mix": {"fp16": 0.2, "int8": 0.3, "int4": 0.5},
+                   "scale_group": wl["group"], "pages": n_pages, "semantics": "quantize_tensor",
+                   "l2": "inputs larger than L2 (15 GB), no flush needed"},
+        "pct_of_hbm_peak": round(100 * gbs / peak, 2),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                     "kernel": "pack_pages_kernel<128,2048,tensor>", "traffic": None,
+                     "algorithmic_bytes_per_launch": read + written, "launch_ms_mean": round(ms, 5)},
+        "e2e": {"value": round(layer_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": 2 * k_host.numel() * 2, "d2h_bytes_per_step": e2e_pool.nbytes,
+                "path": "akv_pack_pages on one layer, K/V from pinned host, records back to pinned host"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        cb = pack_cpu_baseline(args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(cb["gbs"], 4), "unit": "GB/s", "cores": cb["cores"],
+                                "kind": "port", "sample": cb["sample"]}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, wl):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -360,12 +524,25 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="batched")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["pack", "pack_small"], default="batched")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
+    if args.workload in ("pack", "pack_small"):
+        if args.impl == "reference":
+            cb = pack_cpu_baseline(args.cpu_seconds)
+            print(json.dumps({"impl": "reference", "metric": "requantize/pack GB/s (read + written bytes)",
+                              "value": round(cb["gbs"], 4), "unit": "GB/s", "n_gpus": 1,
+                              "higher_is_better": True, "config": {"workload": PACK["name"]},
+                              "cpu_baseline": {"value": round(cb["gbs"], 4), "unit": "GB/s", "cores": cb["cores"],
+                                               "kind": "port", "sample": cb["sample"]},
+                              "e2e": {"value": round(cb["gbs"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}))
+        else:
+            run_pack(args, PACK if args.workload == "pack" else PACK_SMALL)
+        return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, wl)

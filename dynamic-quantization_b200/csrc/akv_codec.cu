@@ -116,6 +116,42 @@ __device__ __forceinline__ uint4 record_load8(int mode, const uint8_t *payload, 
   return make_uint4(h[0], h[1], h[2], h[3]);
 }
 
+// Exact round-half-even of x / s for |x / s| <= 128 without a division per
+// element.  y = x * fl(1/s) is within 2^-16 of the exact quotient there, so
+// rounding y can differ from rounding x / s only when y lies that close to a
+// half-integer; such elements (about 1 in 16000) are redone with the correctly
+// rounded division.  Rounding is the 1.5 * 2^23 magic add (an RN addition).
+// The caller guarantees |x / s| <= qmax * (1 + 2^-11): s is at least the
+// group's absmax / qmax rounded to fp16.  Result clamped to [-qmax, qmax].
+__device__ __forceinline__ float quantize_fast(float x, float s, float r, float qmax) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float y = x * r;
+  float q = (y + kMagic) - kMagic;
+  if (0.5f - fabsf(y - q) <= 3.0517578125e-05f)  // within 2^-15 of a tie: use the exact quotient
+    q = rintf(__fdiv_rn(x, s));
+  return fminf(fmaxf(q, -qmax), qmax);
+}
+// Low bits of an integral float q in [-2^22, 2^22] as two's complement.
+__device__ __forceinline__ uint32_t int_bits(float q) { return __float_as_uint(q + 12582912.0f); }
+// Low bits of 16 q (so bits 4-7 hold q's low nibble): 16 q is exact and added
+// to the same magic in one FMA.
+__device__ __forceinline__ uint32_t int_bits_x16(float q) { return __float_as_uint(fmaf(q, 16.f, 12582912.0f)); }
+
+__device__ __forceinline__ uint32_t hmax2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// max |x| over the 8 fp16 values of a chunk, computed in fp16 (exact).
+__device__ __forceinline__ float chunk_absmax(const uint4 &v) {
+  const uint32_t m = hmax2_u(hmax2_u(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu),
+                             hmax2_u(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
+  return fmaxf(__half2float(__ushort_as_half((unsigned short)(m & 0xffff))),
+               __half2float(__ushort_as_half((unsigned short)(m >> 16))));
+}
+__device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xffff))); }
+__device__ __forceinline__ float half_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+
 // Quantize one slab held in registers (v[c] = 8 fp16 values) into a record.
 template <int D, int G, int SEM>
 __device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], int mode,
@@ -127,19 +163,9 @@ __device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], i
     return;
   }
   const float qmax = mode == AKV_MODE_INT8 ? 127.f : 7.f;
-  float x[NC][8];
   float lm[NC];
 #pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
-    lm[c] = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      x[c][2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xffff)));
-      x[c][2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
-      lm[c] = fmaxf(lm[c], fmaxf(fabsf(x[c][2 * i]), fabsf(x[c][2 * i + 1])));
-    }
-  }
+  for (int c = 0; c < NC; ++c) lm[c] = chunk_absmax(v[c]);
   // Group absmax: G/8 lanes share a group inside a chunk (G < 256), or
   // G/256 whole chunks share one (G >= 256).
   float gm[NC];
@@ -166,26 +192,33 @@ __device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], i
   }
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
-    const GroupScale s = group_scale<SEM>(gm[c], qmax);
-    int q[8];
+    const GroupScale gs = group_scale<SEM>(gm[c], qmax);
+    const float r = __frcp_rn(gs.divisor);
+    const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+    float q[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = quantize_value(x[c][i], s.divisor, qmax);
+    for (int i = 0; i < 4; ++i) {
+      q[2 * i] = quantize_fast(half_lo(w[i]), gs.divisor, r, qmax);
+      q[2 * i + 1] = quantize_fast(half_hi(w[i]), gs.divisor, r, qmax);
+    }
     const int e = 256 * c + 8 * lane;
     if (mode == AKV_MODE_INT8) {
-      uint32_t w0 = 0, w1 = 0;
+      uint32_t b[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        w0 |= (uint32_t)(q[i] & 0xff) << (8 * i);
-        w1 |= (uint32_t)(q[4 + i] & 0xff) << (8 * i);
-      }
+      for (int i = 0; i < 8; ++i) b[i] = int_bits(q[i]);
+      const uint32_t w0 = prmt(prmt(b[0], b[1], 0x0040u), prmt(b[2], b[3], 0x0040u), 0x5410u);
+      const uint32_t w1 = prmt(prmt(b[4], b[5], 0x0040u), prmt(b[6], b[7], 0x0040u), 0x5410u);
       *reinterpret_cast<uint2 *>(payload + e) = make_uint2(w0, w1);
     } else {
-      uint32_t w = 0;
+      uint32_t pb[4];  // byte k: element 2k in the low nibble, 2k+1 in the high nibble
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w |= (uint32_t)(q[i] & 15) << (4 * i);
-      *reinterpret_cast<uint32_t *>(payload + e / 2) = w;
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t lo = int_bits(q[2 * k]), hi = int_bits_x16(q[2 * k + 1]);
+        pb[k] = (lo & 0x0fu) | (hi & 0xf0u);
+      }
+      *reinterpret_cast<uint32_t *>(payload + e / 2) = prmt(prmt(pb[0], pb[1], 0x0040u), prmt(pb[2], pb[3], 0x0040u), 0x5410u);
     }
-    if (e % G == 0) sc[e / G] = s.stored;
+    if (e % G == 0) sc[e / G] = gs.stored;
   }
 }
 
@@ -198,7 +231,7 @@ __device__ __forceinline__ bool page_in_arena(int64_t desc, int64_t page_bytes, 
 // Pack (SRC_RECORD = false: dense fp16 source) or repack (SRC_RECORD = true:
 // source records in the arena) one slab per warp.
 template <int D, int G, int SEM, bool SRC_RECORD>
-__global__ void __launch_bounds__(256) pack_pages_kernel(
+__global__ void __launch_bounds__(256, 3) pack_pages_kernel(
     const __half *__restrict__ src_k, const __half *__restrict__ src_v, int64_t outer_stride,
     int64_t head_stride, int64_t blocks_per_row, const int64_t *__restrict__ src_desc,
     const int64_t *__restrict__ dst_desc, int64_t n_pages, uint8_t *__restrict__ arena,
