@@ -116,41 +116,80 @@ __device__ __forceinline__ uint4 record_load8(int mode, const uint8_t *payload, 
   return make_uint4(h[0], h[1], h[2], h[3]);
 }
 
-// Exact round-half-even of x / s for |x / s| <= 128 without a division per
-// element.  y = x * fl(1/s) is within 2^-16 of the exact quotient there, so
-// rounding y can differ from rounding x / s only when y lies that close to a
-// half-integer; such elements (about 1 in 16000) are redone with the correctly
-// rounded division.  Rounding is the 1.5 * 2^23 magic add (an RN addition).
-// The caller guarantees |x / s| <= qmax * (1 + 2^-11): s is at least the
-// group's absmax / qmax rounded to fp16.  Result clamped to [-qmax, qmax].
-__device__ __forceinline__ float quantize_fast(float x, float s, float r, float qmax) {
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  const float y = x * r;
-  float q = (y + kMagic) - kMagic;
-  if (0.5f - fabsf(y - q) <= 3.0517578125e-05f)  // within 2^-15 of a tie: use the exact quotient
-    q = rintf(__fdiv_rn(x, s));
-  return fminf(fmaxf(q, -qmax), qmax);
+// ---- exact quantization of a page slab without a division per element
+//
+// round-half-even(x / s) for |x / s| <= qmax * (1 + 2^-11) (s is the group's
+// absmax / qmax, possibly rounded down to fp16 by at most 2^-11): y = x * fl(1/s)
+// is within 2^-16 of the exact quotient, so rounding y can differ from rounding
+// x / s only when y lies within that distance of a half-integer.  Rounding is
+// the 1.5 * 2^23 magic add (an RN addition), whose result t carries rint(y) as
+// two's complement in its low mantissa bits.  A chunk where any lane sees a y
+// within 2^-15 of a tie (about 1 chunk in 70 on random data) is redone with the
+// correctly rounded division.  No clamp is needed on the fast path: |y| <=
+// qmax + 0.07 rounds into [-qmax, qmax].
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
 }
-// Low bits of an integral float q in [-2^22, 2^22] as two's complement.
-__device__ __forceinline__ uint32_t int_bits(float q) { return __float_as_uint(q + 12582912.0f); }
-// Low bits of 16 q (so bits 4-7 hold q's low nibble): 16 q is exact and added
-// to the same magic in one FMA.
-__device__ __forceinline__ uint32_t int_bits_x16(float q) { return __float_as_uint(fmaf(q, 16.f, 12582912.0f)); }
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr float kTieGuard = 0.49996948242f;  // 0.5 - 2^-15
 
 __device__ __forceinline__ uint32_t hmax2_u(uint32_t a, uint32_t b) {
   uint32_t d;
   asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+__device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xffff))); }
+__device__ __forceinline__ float half_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
 // max |x| over the 8 fp16 values of a chunk, computed in fp16 (exact).
 __device__ __forceinline__ float chunk_absmax(const uint4 &v) {
   const uint32_t m = hmax2_u(hmax2_u(v.x & 0x7fff7fffu, v.y & 0x7fff7fffu),
                              hmax2_u(v.z & 0x7fff7fffu, v.w & 0x7fff7fffu));
-  return fmaxf(__half2float(__ushort_as_half((unsigned short)(m & 0xffff))),
-               __half2float(__ushort_as_half((unsigned short)(m >> 16))));
+  return fmaxf(half_lo(m), half_hi(m));
 }
-__device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xffff))); }
-__device__ __forceinline__ float half_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+
+// Quantize the 8 fp16 values of a chunk; returns their integers' low bytes in
+// t[i] (bits 0-7 two's complement).
+__device__ __forceinline__ void quantize_chunk(const uint4 &v, float s, float r, float qmax,
+                                               uint32_t (&t)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const uint64_t r2 = f2_pack(r, r), magic2 = f2_pack(kRoundMagic, kRoundMagic);
+  bool tie = false;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint64_t y = f2_mul(f2_pack(half_lo(w[i]), half_hi(w[i])), r2);
+    const uint64_t tt = f2_add(y, magic2);
+    const uint64_t d = f2_sub(y, f2_sub(tt, magic2));
+    tie |= fabsf(f2_lo(d)) >= kTieGuard;
+    tie |= fabsf(f2_hi(d)) >= kTieGuard;
+    t[2 * i] = (uint32_t)tt;
+    t[2 * i + 1] = (uint32_t)(tt >> 32);
+  }
+  if (__any_sync(0xffffffffu, tie)) {  // rare: recompute the chunk with the exact quotient
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float x = (i & 1) ? half_hi(w[i >> 1]) : half_lo(w[i >> 1]);
+      const float q = fminf(fmaxf(rintf(__fdiv_rn(x, s)), -qmax), qmax);
+      t[i] = __float_as_uint(q + kRoundMagic);
+    }
+  }
+}
 
 // Quantize one slab held in registers (v[c] = 8 fp16 values) into a record.
 template <int D, int G, int SEM>
@@ -190,33 +229,27 @@ __device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], i
       for (int c = c0; c < c0 + CPG; ++c) gm[c] = m;
     }
   }
+  GroupScale gs{};
+  float r = 0.f;
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
-    const GroupScale gs = group_scale<SEM>(gm[c], qmax);
-    const float r = __frcp_rn(gs.divisor);
-    const uint32_t w[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
-    float q[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      q[2 * i] = quantize_fast(half_lo(w[i]), gs.divisor, r, qmax);
-      q[2 * i + 1] = quantize_fast(half_hi(w[i]), gs.divisor, r, qmax);
+    if (c == 0 || G < 256 || c % (G / 256) == 0) {  // a new group starts in this chunk
+      gs = group_scale<SEM>(gm[c], qmax);
+      r = __frcp_rn(gs.divisor);
     }
+    uint32_t t[8];
+    quantize_chunk(v[c], gs.divisor, r, qmax, t);
     const int e = 256 * c + 8 * lane;
     if (mode == AKV_MODE_INT8) {
-      uint32_t b[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) b[i] = int_bits(q[i]);
-      const uint32_t w0 = prmt(prmt(b[0], b[1], 0x0040u), prmt(b[2], b[3], 0x0040u), 0x5410u);
-      const uint32_t w1 = prmt(prmt(b[4], b[5], 0x0040u), prmt(b[6], b[7], 0x0040u), 0x5410u);
+      const uint32_t w0 = prmt(prmt(t[0], t[1], 0x0040u), prmt(t[2], t[3], 0x0040u), 0x5410u);
+      const uint32_t w1 = prmt(prmt(t[4], t[5], 0x0040u), prmt(t[6], t[7], 0x0040u), 0x5410u);
       *reinterpret_cast<uint2 *>(payload + e) = make_uint2(w0, w1);
     } else {
       uint32_t pb[4];  // byte k: element 2k in the low nibble, 2k+1 in the high nibble
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t lo = int_bits(q[2 * k]), hi = int_bits_x16(q[2 * k + 1]);
-        pb[k] = (lo & 0x0fu) | (hi & 0xf0u);
-      }
-      *reinterpret_cast<uint32_t *>(payload + e / 2) = prmt(prmt(pb[0], pb[1], 0x0040u), prmt(pb[2], pb[3], 0x0040u), 0x5410u);
+      for (int k = 0; k < 4; ++k) pb[k] = (t[2 * k] & 0x0fu) | ((t[2 * k + 1] << 4) & 0xf0u);
+      *reinterpret_cast<uint32_t *>(payload + e / 2) =
+          prmt(prmt(pb[0], pb[1], 0x0040u), prmt(pb[2], pb[3], 0x0040u), 0x5410u);
     }
     if (e % G == 0) sc[e / G] = gs.stored;
   }
