@@ -57,6 +57,15 @@ WORKLOADS = {
 }
 
 
+# One sequence of 1,048,576 tokens (65,536 pages), 32 query / 8 KV heads,
+# 5/25/70 FP16/INT8/INT4, split contiguously across the GPUs (strong scaling):
+# each rank decodes its shard into LSE states, NCCL all-gathers them, every
+# rank merges.  A step is one layer's decode of the whole context.
+LONG = dict(
+    name="long-context single-sequence decode, 1,048,576 tokens, sequence-sharded",
+    layers=1, q_heads=32, kv_heads=8, dim=128, batch=1, tokens=1 << 20,
+    mix={16: 0.05, 8: 0.25, 4: 0.70}, group=2048)
+
 PACK = dict(
     name="requantize/pack, 28 layers x 32 sequences x 8 KV heads x 4096 tokens x 128 dims",
     layers=28, batch=32, kv_heads=8, tokens=4096, dim=128, group=2048,
@@ -72,9 +81,10 @@ def hbm_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def traffic_from_profile(workload: str):
-    """DRAM bytes per decode launch from the committed ncu summary, if present."""
-    f = ROOT / "profiles" / f"decode_partials_{workload}.txt"
+def traffic_from_profile(name: str):
+    """DRAM bytes per launch from the committed ncu summary ``profiles/<name>.md``
+    (its ``traffic_bytes_per_launch:`` line), if present."""
+    f = ROOT / "profiles" / f"{name}.md"
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
@@ -131,7 +141,10 @@ def cpu_baseline(wl: dict, seed: int, seconds: float, calls_min: int = 3):
 
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    blocks = wl["tokens"] // 16
+    # Contexts beyond 65,536 tokens are timed on a 65,536-token contiguous slice;
+    # tokens/s is scaled by the number of slices.
+    blocks = min(wl["tokens"], 65536) // 16
+    slices = wl["tokens"] // (blocks * 16)
     bits = OB.random_bits(seed, blocks, wl["mix"])
     pages = OB.build_sequence(seed, wl["kv_heads"], wl["dim"], blocks, bits, wl["group"])
     q = torch.randn(1, wl["q_heads"], 1, wl["dim"], generator=torch.Generator().manual_seed(seed)).half()
@@ -145,14 +158,14 @@ def cpu_baseline(wl: dict, seed: int, seconds: float, calls_min: int = 3):
         times.append(time.perf_counter() - t0)
     per_call = statistics.median(times)
     nbytes = OB.resident_bytes(pages) + 2 * q.numel() * 2
-    calls_per_step = wl["layers"] * wl["batch"]
+    calls_per_step = wl["layers"] * wl["batch"] * slices
     return {
         "gbs": nbytes / per_call / 1e9,
         "tokens_per_s": wl["batch"] / (per_call * calls_per_step),
         "cores": cores,
         "calls": len(times),
         "seconds_per_call": per_call,
-        "sample": (f"{len(times)} decode calls of one sequence-layer ({blocks} pages, "
+        "sample": (f"{len(times)} decode calls of one sequence-layer slice ({blocks} pages, "
                    f"{wl['kv_heads']} KV heads, same precision mix), median per call; "
                    f"tokens/s extrapolated x{calls_per_step} calls per step"),
     }
@@ -296,7 +309,7 @@ def run_ours(args, wl):
         gbs = total_bytes / (ms * 1e-3) / 1e9
         tokens = B * world / (ms * 1e-3)
         achieved = (step_bytes / L) / (dec_ms_mean * 1e-3) / 1e9
-        traffic = traffic_from_profile(args.workload)
+        traffic = traffic_from_profile(f"decode_streamk_{args.workload}")
         line = {
             "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -479,7 +492,8 @@ def run_pack(args, wl):
         "pct_of_hbm_peak": round(100 * gbs / peak, 2),
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gbs / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                     "kernel": "pack_pages_kernel<128,2048,tensor>", "traffic": None,
+                     "kernel": "pack_pages_kernel<128,2048,tensor>",
+                     "traffic": traffic_from_profile("pack_pages_pack") if wl is PACK else None,
                      "algorithmic_bytes_per_launch": read + written, "launch_ms_mean": round(ms, 5)},
         "e2e": {"value": round(layer_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": 2 * k_host.numel() * 2, "d2h_bytes_per_step": e2e_pool.nbytes,
@@ -492,6 +506,152 @@ def run_pack(args, wl):
         line["cpu_baseline"] = {"value": round(cb["gbs"], 4), "unit": "GB/s", "cores": cb["cores"],
                                 "kind": "port", "sample": cb["sample"]}
     print(json.dumps(line), flush=True)
+
+
+def run_long(args, wl):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import anchorkv_b200 as akv
+    from anchorkv_b200 import _lib
+    from anchorkv_b200 import pool as P
+    from anchorkv_b200.sharded import gather_states, shard_range
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    Hq, Hkv, D = wl["q_heads"], wl["kv_heads"], wl["dim"]
+    nblk = wl["tokens"] // 16
+    lo, hi = shard_range(nblk, rank, world)
+    rng = np.random.default_rng(1000 + rank)
+    keys = list(wl["mix"])
+    bits = rng.choice(np.array(keys), size=(1, hi - lo), p=[wl["mix"][k] for k in keys])
+    pool = P.PagePool(Hkv, D, group=wl["group"], pages={b: int((bits == b).sum()) for b in (16, 8, 4)},
+                      device=device, shuffle_seed=rank, zero=False)
+    gen = torch.Generator(device=device).manual_seed(77 + rank)
+    k = torch.empty((1, Hkv, (hi - lo) * 16, D), dtype=torch.float16, device=device).normal_(generator=gen)
+    v = torch.empty_like(k).normal_(generator=gen)
+    store = P.pack_dense(pool, k, v, bits, semantics="tensor")
+    del k, v
+    qgen = torch.Generator(device=device).manual_seed(5)  # the same query on every rank
+    q = torch.randn((1, Hq, 1, D), generator=qgen, device=device, dtype=torch.float32).half()
+    kv_bytes = store.resident_bytes()
+    scale = 1 / math.sqrt(D)
+    lib = _lib.load()
+    ws_bytes = lib.akv_workspace_bytes(1, Hq, Hkv, D, hi - lo, 0)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
+    state = torch.empty((1, Hq, D + 2), dtype=torch.float32, device=device)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(device)
+    status = _lib.status_word(device)
+    torch.cuda.synchronize(device)
+
+    def step(ev=None, i=0):
+        if ev is not None:
+            ev[0][i].record(stream)
+        assert lib.akv_decode_partials(pool.arena.data_ptr(), pool.nbytes, store.table.data_ptr(),
+                                       store.table.stride(0), store.seq_blocks.data_ptr(), store.max_blocks,
+                                       q.data_ptr(), q.stride(0), q.stride(1), 1, Hq, Hkv, D, wl["group"], scale,
+                                       0, ws.data_ptr(), ws_bytes, status.data_ptr(), stream.cuda_stream) == 0
+        if ev is not None:
+            ev[1][i].record(stream)
+        assert lib.akv_merge(ws.data_ptr(), 1, Hq, D, None, 0, 0, state.data_ptr(), status.data_ptr(),
+                             stream.cuda_stream) == 0
+        states = gather_states(state) if world > 1 else state.unsqueeze(0)
+        assert lib.akv_merge_states(states.data_ptr(), world, 1, Hq, D, out.data_ptr(), out.stride(0),
+                                    out.stride(1), stream.cuda_stream) == 0
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    ev = ([torch.cuda.Event(enable_timing=True) for _ in range(args.steps)],
+          [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)])
+    gpu_id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    sampler = ClockSampler(gpu_id)
+    time.sleep(0.3)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(ev, i)
+    t1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    assert akv.take_device_status(device) == 0
+    ms_local = t0.elapsed_time(t1) / args.steps
+    dec_ms = sum(a.elapsed_time(b) for a, b in zip(*ev)) / args.steps
+
+    # end to end: the query from pinned host memory, the output back to it
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+
+    def e2e_step():
+        q.copy_(q_host, non_blocking=True)
+        step()
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(max(10, args.steps // 4)):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms_local = e0.elapsed_time(e1) / max(10, args.steps // 4)
+    totals = torch.tensor([ms_local, e2e_ms_local, dec_ms, float(kv_bytes)], dtype=torch.float64, device=device)
+    if world > 1:
+        mx = totals[:3].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        kv_all = totals[3:].clone()
+        dist.all_reduce(kv_all, op=dist.ReduceOp.SUM)
+        ms, e2e_ms, dec_ms_max = mx.tolist()
+        kv_total = kv_all.item()
+    else:
+        ms, e2e_ms, dec_ms_max = ms_local, e2e_ms_local, dec_ms
+        kv_total = float(kv_bytes)
+    if rank == 0:
+        peak, peak_kind = hbm_peak()
+        step_bytes = kv_total + 2 * q.numel() * 2
+        gbs = step_bytes / (ms * 1e-3) / 1e9
+        achieved = (kv_bytes + 2 * q.numel() * 2) / (dec_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 operands, f32 accumulation", "data": "synthetic (seeded fp16 N(0,1))",
+            "config": {"workload": wl["name"], "q_heads": Hq, "kv_heads": Hkv, "head_dim": D,
+                       "context_tokens": wl["tokens"], "page_tokens": 16,
+                       "precision_mix": {"fp16": 0.05, "int8": 0.25, "int4": 0.70}, "scale_group": wl["group"],
+                       "parallelism": f"sequence-sharded x{world}, NCCL all-gather of LSE states",
+                       "collective_bytes_per_rank": state.numel() * 4,
+                       "l2": "inputs larger than L2 (1.5 GB of KV), no flush needed"},
+            "tokens_per_s": round(1 / (ms * 1e-3), 1),
+            "pct_of_hbm_peak": round(100 * gbs / world / peak, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                         "kernel": "decode_streamk_kernel<128>", "traffic": None,
+                         "launch_ms_mean": round(dec_ms, 5), "launch_ms_max_over_ranks": round(dec_ms_max, 5)},
+            "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": q.numel() * 2,
+                    "d2h_bytes_per_step": out.numel() * 2},
+            "gpu_launches": args.steps * 3,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
 
 
 def run_reference(args, wl):
@@ -524,7 +684,7 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["pack", "pack_small"], default="batched")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["long", "pack", "pack_small"], default="batched")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -542,6 +702,12 @@ def main():
                                       "d2h_bytes_per_step": 0}}))
         else:
             run_pack(args, PACK if args.workload == "pack" else PACK_SMALL)
+        return
+    if args.workload == "long":
+        if args.impl == "reference":
+            run_reference(args, dict(LONG, layers=1, batch=1, splits=0))
+        else:
+            run_long(args, LONG)
         return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":

@@ -34,7 +34,8 @@ from .backend import (
 from .decode import decode_partial_states, merge_states, packed_attention
 from .packed_decode import PagedLayer, QuantizedPage, dense_attention, kl_divergence, pack_page, tensor_bytes
 from .policy import CacheMode, CachePlan, PlannedSegment
-from .pool import PagedBatch, PagePool
+from .pool import PagedBatch, PagePool, pack_dense
+from .sharded import gather_states, shard_range, sharded_packed_attention
 from ._lib import KernelError, NativeUnavailableError, take_device_status
 
 __version__ = "0.1.0"
@@ -46,5 +47,6 @@ __all__ = [
     "PackedTensor", "PagePool", "PagedBatch", "PagedLayer", "PlannedSegment", "QuantizedPage",
     "SegmentRecord", "SegmentRole", "decode_partial_states", "dense_attention", "kl_divergence",
     "merge_states", "pack_page", "packed_attention", "quantize_tensor", "stack_legacy_cache",
-    "take_device_status", "tensor_bytes",
+    "take_device_status", "tensor_bytes", "pack_dense", "shard_range", "gather_states",
+    "sharded_packed_attention",
 ]

@@ -51,7 +51,7 @@ struct DecodeTraits {
   static constexpr int DK = D / 4;     // K dims a lane owns per row
   static constexpr int DV = D / 8;     // V dims a lane owns per row
   static constexpr int kTiles = D / 16;
-  static constexpr int kSmem = kWarps * kRing + kWarps * kSlots * (8 + 4 + 4);
+  static constexpr int kSmem = kWarps * kRing + kWarps * kSlots * (8 + 4 + 4 + 4);
   static_assert(kRing % 16 == 0 && kRing >= 4 * kBlock * D, "a ring must hold one FP16 record");
 };
 
@@ -388,6 +388,7 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
   uint32_t *slot_start = reinterpret_cast<uint32_t *>(smem + T::kWarps * T::kRing +
                                                       T::kWarps * T::kSlots * 8) + warp * T::kSlots;
   uint32_t *slot_meta = slot_start + T::kWarps * T::kSlots;
+  uint32_t *slot_phys = slot_meta + T::kWarps * T::kSlots;
 
   const int lg = p.log2_group;
   ScaleIdx si;
@@ -454,7 +455,7 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
     prepare(win0, raw, nb);
   }
 
-  uint32_t head = 0, tail = 0;  // virtual byte counters of the ring
+  uint32_t head = 0, tail = 0, head_p = 0;  // ring counters (virtual) and write position
   int issued = 0, consumed = 0;
   bool timed_out = false;
 
@@ -480,21 +481,22 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
     const int item = first_item + seg;
     const int qg = (item % ipb) % p.qgroups;
     const int nq = min(8, p.gqa - 8 * qg);
-    float *base = p.partials + ((int64_t)gw * p.smax + seg) * p.slot_heads * (D + 2);
+    constexpr int PS = D + 4;  // partial row: acc[D], m, l, 2 pad (16-byte aligned rows)
+    float *base = p.partials + ((int64_t)gw * p.smax + seg) * p.slot_heads * PS;
     // Scalar stores: the accumulators stay in the MMA's register quads (a
     // float2 pairing of (c0, c2) would fight that allocation on every page).
     const int h0 = 2 * t4, h1 = 2 * t4 + 1;
     if (h0 < nq) {
-      float *row = base + h0 * (D + 2) + T::DV * gid;
+      float *row = base + h0 * PS + T::DV * gid;
 #pragma unroll
       for (int m = 0; m < T::kTiles; ++m) row[2 * m] = o[m][0], row[2 * m + 1] = o[m][2];
-      if (gid == 0) base[h0 * (D + 2) + D] = st.m0, base[h0 * (D + 2) + D + 1] = l0;
+      if (gid == 0) base[h0 * PS + D] = st.m0, base[h0 * PS + D + 1] = l0;
     }
     if (h1 < nq) {
-      float *row = base + h1 * (D + 2) + T::DV * gid;
+      float *row = base + h1 * PS + T::DV * gid;
 #pragma unroll
       for (int m = 0; m < T::kTiles; ++m) row[2 * m] = o[m][1], row[2 * m + 1] = o[m][3];
-      if (gid == 0) base[h1 * (D + 2) + D] = st.m1, base[h1 * (D + 2) + D + 1] = l1;
+      if (gid == 0) base[h1 * PS + D] = st.m1, base[h1 * PS + D + 1] = l1;
     }
   };
   auto next_segment = [&]() {
@@ -523,15 +525,17 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
       }
       const int k = __ffs(w_mask) - 1;
       const uint32_t rb = __shfl_sync(0xffffffffu, w_rb, k);
-      // Virtual byte counters grow monotonically (a warp moves far less than
-      // 4 GB per launch); the physical offset is mod kRing.
-      uint32_t start = head;
-      const uint32_t phys = start % (uint32_t)T::kRing;
-      if (issued == consumed && phys != 0) {  // empty ring: restart at a lap boundary
-        start += T::kRing - phys;
+      // Ring space: virtual byte counters (head, tail) grow monotonically (a
+      // warp moves far less than 4 GB per launch) and measure occupancy; the
+      // physical write position head_p is tracked beside them (no modulo).
+      uint32_t start = head, start_p = head_p;
+      if (issued == consumed && start_p != 0) {  // empty ring: restart at a lap boundary
+        start += T::kRing - start_p;
+        start_p = 0;
         tail = start;
-      } else if (phys + rb > (uint32_t)T::kRing) {
-        start += T::kRing - phys;  // wrap to the next lap
+      } else if (start_p + rb > (uint32_t)T::kRing) {  // wrap to the next lap
+        start += T::kRing - start_p;
+        start_p = 0;
       }
       if (start + rb - tail > (uint32_t)T::kRing) break;  // wait for room
       const int64_t src = __shfl_sync(0xffffffffu, w_src, k);
@@ -539,13 +543,15 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
       const int slot = issued % T::kSlots;
       if (lane == 0) {
         slot_start[slot] = start;
+        slot_phys[slot] = start_p;
         slot_meta[slot] = meta;
         fence_proxy_async_smem();  // prior generic reads of this space before the async write
         const uint32_t bar = smem_u32(&bars[slot]);
         mbar_expect_tx(bar, rb);
-        bulk_g2s(smem_u32(ring + start % (uint32_t)T::kRing), p.arena + src, rb, bar);
+        bulk_g2s(smem_u32(ring + start_p), p.arena + src, rb, bar);
       }
       head = start + rb;
+      head_p = start_p + rb;
       ++issued;
       w_mask &= w_mask - 1;
     }
@@ -558,7 +564,7 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
       break;
     }
     const uint32_t meta = slot_meta[slot];
-    uint8_t *rec = ring + slot_start[slot] % (uint32_t)T::kRing;
+    uint8_t *rec = ring + slot_phys[slot];
     const int seg = (int)(meta >> 16);
     while (cur_seg < seg) {
       finalize(cur_seg);
@@ -595,13 +601,19 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
 }
 
 // Merge the partial states of the warps that touched each (sequence, query
-// head).  One CTA of head_dim threads per (query head, sequence).
+// head).  One CTA of 4 warps per (query head, sequence): warp w folds
+// contributors w, w+4, ... with a single-pass online LSE merge (each lane owns
+// D/32 dims, loaded as one vector), then the 4 warps combine in shared memory.
+// A long single sequence has hundreds of contributors per head; a batch has
+// two or three.
 template <int D>
-__global__ void __launch_bounds__(D) merge_kernel(const int32_t *__restrict__ header,
-                                                  const float *__restrict__ partials,
-                                                  __half *__restrict__ out, int64_t obs, int64_t ohs,
-                                                  float *__restrict__ state, int32_t *status) {
-  constexpr int RS = D + 2;
+__global__ void __launch_bounds__(128) merge_kernel(const int32_t *__restrict__ header,
+                                                    const float *__restrict__ partials,
+                                                    __half *__restrict__ out, int64_t obs, int64_t ohs,
+                                                    float *__restrict__ state, int32_t *status) {
+  constexpr int PS = D + 4, VEC = D / 32, RS = D + 2;
+  __shared__ float sm_acc[4][D];
+  __shared__ float sm_m[4], sm_l[4];
   if (header[kMagic] != kHeaderMagic || header[kHeadDimF] != D) {
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
     return;
@@ -609,34 +621,73 @@ __global__ void __launch_bounds__(D) merge_kernel(const int32_t *__restrict__ he
   const int warps = header[kWarpsF], smax = header[kSmaxF], range = header[kRangeF];
   const int mb = header[kMaxBlocksF], kv_heads = header[kKvHeadsF], qgroups = header[kQGroupsF];
   const int gqa = header[kGqaF], slot_heads = header[kSlotHeadsF];
-  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = h / gqa, r = h - kvh * gqa, qg = r >> 3, n = r & 7;
   const int64_t item = ((int64_t)b * kv_heads + kvh) * qgroups + qg;
-  int64_t w0 = 0, w1 = -1;
+  float m = -INFINITY, l = 0.f, acc[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
   if (mb > 0) {
-    w0 = item * mb / range;
-    w1 = ((item + 1) * mb - 1) / range;
-    if (w1 > warps - 1) w1 = warps - 1;
+    const int64_t w0 = item * mb / range;
+    const int64_t w1 = min(((item + 1) * mb - 1) / range, (int64_t)warps - 1);
+    int64_t w = w0 + warp;
+    if (w <= w1) {
+      // first item of contributor w, advanced incrementally by 4 contributors
+      int64_t first = w * range / mb, rem = w * range - first * mb;
+      const int64_t stride = 4ll * range, sq = stride / mb, sr = stride - sq * mb;
+#pragma unroll 2
+      for (; w <= w1; w += 4) {
+        const float *pr = partials + ((w * smax + (item - first)) * slot_heads + n) * PS;
+        const float mw = pr[D], lw = pr[D + 1];
+        float a[VEC];
+        if constexpr (VEC == 4) {
+          const float4 v = *reinterpret_cast<const float4 *>(pr + 4 * lane);
+          a[0] = v.x, a[1] = v.y, a[2] = v.z, a[3] = v.w;
+        } else {
+          const float2 v = *reinterpret_cast<const float2 *>(pr + 2 * lane);
+          a[0] = v.x, a[1] = v.y;
+        }
+        if (mw != -INFINITY) {  // an empty share weighs 0 (triton_decode.py:78)
+          if (mw > m) {
+            const float c = ex2(m - mw);
+            l *= c;
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) acc[i] *= c;
+            m = mw;
+          }
+          const float e = ex2(mw - m);
+          l += e * lw;
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) acc[i] += e * a[i];
+        }
+        first += sq, rem += sr;
+        if (rem >= mb) rem -= mb, ++first;
+      }
+    }
   }
-  float top = -INFINITY;
-  for (int64_t w = w0; w <= w1; ++w) {
-    const int64_t seg = item - (w * range) / mb;
-    top = fmaxf(top, partials[((w * smax + seg) * slot_heads + n) * RS + D]);
-  }
-  float num = 0.f, den = 0.f;
-  for (int64_t w = w0; w <= w1; ++w) {
-    const int64_t seg = item - (w * range) / mb;
-    const float *pr = partials + ((w * smax + seg) * slot_heads + n) * RS;
-    const float m = pr[D];
-    const float wt = m == -INFINITY ? 0.f : ex2(m - top);  // empty share weighs 0 (triton_decode.py:78)
-    num += wt * pr[d];
-    den += wt * pr[D + 1];
-  }
-  if (out) out[(int64_t)b * obs + (int64_t)h * ohs + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
-  if (state) {
-    float *st = state + ((int64_t)b * gridDim.x + h) * RS;
-    st[d] = num;
-    if (d == 0) st[D] = top, st[D + 1] = den;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) sm_acc[warp][VEC * lane + i] = acc[i];
+  if (lane == 0) sm_m[warp] = m, sm_l[warp] = l;
+  __syncthreads();
+  const int d = threadIdx.x;
+  if (d < D) {
+    float top = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) top = fmaxf(top, sm_m[k]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float e = sm_m[k] == -INFINITY ? 0.f : ex2(sm_m[k] - top);
+      num += e * sm_acc[k][d];
+      den += e * sm_l[k];
+    }
+    if (out) out[(int64_t)b * obs + (int64_t)h * ohs + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+    if (state) {
+      float *st = state + ((int64_t)b * gridDim.x + h) * RS;
+      st[d] = num;
+      if (d == 0) st[D] = top, st[D + 1] = den;
+    }
   }
 }
 
@@ -716,7 +767,7 @@ static int make_plan(int batch, int q_heads, int kv_heads, int head_dim, int max
   pl.warps = (int)warps;
   pl.smax = max_blocks > 0 ? (int)(1 + (range - 1 + max_blocks - 1) / max_blocks) : 1;
   pl.ctas = (int)((warps + DecodeTraits<128>::kWarps - 1) / DecodeTraits<128>::kWarps);
-  pl.bytes = kHeaderBytes + (int64_t)pl.warps * pl.smax * pl.slot_heads * (head_dim + 2) * 4;
+  pl.bytes = kHeaderBytes + (int64_t)pl.warps * pl.smax * pl.slot_heads * (head_dim + 4) * 4;
   *plan = pl;
   return AKV_OK;
 }
@@ -803,8 +854,8 @@ extern "C" int akv_merge(const void *workspace, int32_t batch, int32_t q_heads, 
   const dim3 grid(q_heads, batch);
   cudaStream_t s = (cudaStream_t)stream;
   if (head_dim == 64)
-    merge_kernel<64><<<grid, 64, 0, s>>>(header, partials, (__half *)out, out_batch_stride,
-                                         out_head_stride, state_out, dev_status);
+    merge_kernel<64><<<grid, 128, 0, s>>>(header, partials, (__half *)out, out_batch_stride,
+                                          out_head_stride, state_out, dev_status);
   else
     merge_kernel<128><<<grid, 128, 0, s>>>(header, partials, (__half *)out, out_batch_stride,
                                            out_head_stride, state_out, dev_status);
