@@ -15,7 +15,7 @@
 //    window ahead, a ballot marks the pages to copy), skips evicted or
 //    invisible pages without reading them, and bulk-copies each record
 //    (cp.async.bulk, mbarrier completion, no multicast; lane 0 issues) into a
-//    private 16 KB shared-memory ring the moment it frees room, so the copy
+//    private 12 KB shared-memory ring the moment it frees room, so the copy
 //    pipeline needs no hand-off between warps;
 //  * a warp serves every query head of its KV head (up to 8 per pass; the
 //    reference re-reads each KV page once per query head);
@@ -23,6 +23,8 @@
 //    fragments (exact: the integer is formed in fp16 by an exponent trick and
 //    multiplied by the fp16 scale with one rounding, matching
 //    fp16(int * float(scale)) of packed_decode.py:45 / triton_decode.py:31);
+//    with one scale per page (group = 16 * head_dim) the V scale is instead
+//    multiplied into the page's fp16 P fragment, one rounding per term as well;
 //  * Q.K^T and P.V run as mma.sync m16n8k16 (f16 x f16 -> f32): 16 tokens x 8
 //    query heads per page, 2 * head_dim/16 MMAs per page;
 //  * the online softmax is fp32 in base 2; the running max only moves (one
@@ -198,7 +200,8 @@ __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, c
 // DV*gid + [0, DV): m-tile m's A rows gid / gid+8 are dims DV*gid + 2m / +2m+1;
 // its k (token) columns 2t4, 2t4+1 / 2t4+8, 2t4+9 match the P fragment that
 // movmatrix produced from the score accumulators.
-template <int D, int MODE, bool SLAB>
+// FOLD: the page has a single V scale, already multiplied into P.
+template <int D, int MODE, bool SLAB, bool FOLD>
 __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, const ScaleIdx &si,
                                         int gid, int t4, uint32_t b0, uint32_t b1,
                                         float (&o)[D / 16][4]) {
@@ -210,8 +213,9 @@ __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, 
   constexpr int WP = W / PARTS;
   constexpr int TP = (D / 16) / PARTS;        // m-tiles per part
   const uint8_t *base = vrec + gid * (W * 4);
+  auto sc = [](uint32_t x, uint32_t s) { return FOLD ? x : hmul2(x, s); };
   uint32_t sab = 0, scd = 0;
-  if constexpr (MODE != AKV_MODE_FP16) {
+  if constexpr (MODE != AKV_MODE_FP16 && !FOLD) {
     if constexpr (SLAB) {
       sab = scd = rep_half(vsc);
     } else {
@@ -236,8 +240,8 @@ __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, 
         for (int mm = 0; mm < 4; ++mm) {
           const uint32_t ab = (mm < 2 ? xab : yab) >> (8 * (mm & 1));
           const uint32_t cd = (mm < 2 ? xcd : ycd) >> (8 * (mm & 1));
-          mma_16816(op[4 * q + mm], hmul2(int4_lo_to_f16x2(ab), sab), hmul2(int4_hi_to_f16x2(ab), sab),
-                    hmul2(int4_lo_to_f16x2(cd), scd), hmul2(int4_hi_to_f16x2(cd), scd), b0, b1);
+          mma_16816(op[4 * q + mm], sc(int4_lo_to_f16x2(ab), sab), sc(int4_hi_to_f16x2(ab), sab),
+                    sc(int4_lo_to_f16x2(cd), scd), sc(int4_hi_to_f16x2(cd), scd), b0, b1);
         }
       }
     } else if constexpr (MODE == AKV_MODE_INT8) {
@@ -246,10 +250,10 @@ __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, 
 #pragma unroll
         for (int mm = 0; mm < 2; ++mm) {
           const uint32_t lo = sel8(2 * mm), hi = sel8(2 * mm + 1);
-          mma_16816(op[2 * q + mm], hmul2(int8_to_f16x2(prmt(wa[q], wb[q], lo)), sab),
-                    hmul2(int8_to_f16x2(prmt(wa[q], wb[q], hi)), sab),
-                    hmul2(int8_to_f16x2(prmt(wc[q], wd[q], lo)), scd),
-                    hmul2(int8_to_f16x2(prmt(wc[q], wd[q], hi)), scd), b0, b1);
+          mma_16816(op[2 * q + mm], sc(int8_to_f16x2(prmt(wa[q], wb[q], lo)), sab),
+                    sc(int8_to_f16x2(prmt(wa[q], wb[q], hi)), sab),
+                    sc(int8_to_f16x2(prmt(wc[q], wd[q], lo)), scd),
+                    sc(int8_to_f16x2(prmt(wc[q], wd[q], hi)), scd), b0, b1);
         }
       }
     } else {
@@ -265,10 +269,12 @@ struct SoftmaxState {
   float m0, m1, l0, l1;  // heads 2t4, 2t4+1: running max (base 2) and this lane's sum
 };
 
-// Online softmax of one page's scores; returns the fp16 P fragments for P.V.
+// Online softmax of one page's scores; returns the fp16 P fragments for P.V,
+// multiplied by `pscale` (the page's V scale when it is folded into P; the
+// running sums take the unscaled P).
 template <int D>
 __device__ __forceinline__ void page_softmax(float (&s)[4], int ntok, int gid, float scale_log2,
-                                             SoftmaxState &st, float (&o)[D / 16][4],
+                                             float pscale, SoftmaxState &st, float (&o)[D / 16][4],
                                              uint32_t &b0, uint32_t &b1) {
   constexpr float kNegInf = -INFINITY;
   if (ntok < kBlock) {  // tokens past the page's valid count do not exist
@@ -297,8 +303,8 @@ __device__ __forceinline__ void page_softmax(float (&s)[4], int ntok, int gid, f
   const float p2 = ex2(fmaf(s[2], scale_log2, -st.m0));
   const float p3 = ex2(fmaf(s[3], scale_log2, -st.m1));
   st.l0 += p0 + p2, st.l1 += p1 + p3;
-  b0 = movmatrix_trans(pack_f16x2(p0, p1));
-  b1 = movmatrix_trans(pack_f16x2(p2, p3));
+  b0 = movmatrix_trans(pack_f16x2(p0 * pscale, p1 * pscale));
+  b1 = movmatrix_trans(pack_f16x2(p2 * pscale, p3 * pscale));
 }
 
 template <int D, int MODE, bool SLAB>
@@ -318,10 +324,27 @@ __device__ __forceinline__ void page_attend(uint8_t *rec, int ntok, int lane, in
   const __half *ksc = reinterpret_cast<const __half *>(rec + 2 * PB);
   const __half *vsc = ksc + (SLAB ? 1 : ((kBlock * D) >> log2_group));
   float s[4];
-  page_qk<D, MODE, SLAB>(rec, ksc, si, gid, t4, qf, s);
   uint32_t b0, b1;
-  page_softmax<D>(s, ntok, gid, scale_log2, st, o, b0, b1);
-  page_pv<D, MODE, SLAB>(rec + PB, vsc, si, gid, t4, b0, b1, o);
+  if constexpr (SLAB && MODE != AKV_MODE_FP16) {
+    // One V scale per page: P.V = (P * sV) . v_int, so no V element is
+    // multiplied by its scale (the rounding moves from fp16(int * sV) to
+    // fp16(P * sV), both one fp16 rounding per term).  K keeps the reference's
+    // per-element fp16(int * sK): the scores amplify that rounding through exp.
+    // P <= 2^8 (lazy softmax), so P * sV stays finite in fp16 while sV <= 255;
+    // larger V scales (values beyond +-1785 in INT4) take the per-element path.
+    const float sv = __half2float(*vsc);
+    page_qk<D, MODE, SLAB>(rec, ksc, si, gid, t4, qf, s);
+    const bool fold_v = sv <= 255.f;
+    page_softmax<D>(s, ntok, gid, scale_log2, fold_v ? sv : 1.f, st, o, b0, b1);
+    if (fold_v)
+      page_pv<D, MODE, SLAB, true>(rec + PB, vsc, si, gid, t4, b0, b1, o);
+    else
+      page_pv<D, MODE, SLAB, false>(rec + PB, vsc, si, gid, t4, b0, b1, o);
+  } else {
+    page_qk<D, MODE, SLAB>(rec, ksc, si, gid, t4, qf, s);
+    page_softmax<D>(s, ntok, gid, scale_log2, 1.f, st, o, b0, b1);
+    page_pv<D, MODE, SLAB, false>(rec + PB, vsc, si, gid, t4, b0, b1, o);
+  }
 }
 
 // Query words of this lane for item `item`: DK dims of query head (first head of
