@@ -15,8 +15,11 @@
 //    window ahead, a ballot marks the pages to copy), skips evicted or
 //    invisible pages without reading them, and bulk-copies each record
 //    (cp.async.bulk, mbarrier completion, no multicast; lane 0 issues) into a
-//    private 12 KB shared-memory ring the moment it frees room, so the copy
+//    private 13 KB shared-memory ring the moment it frees room, so the copy
 //    pipeline needs no hand-off between warps;
+//  * INT8 and INT4 pages travel in pairs (two pages of one item and mode, one
+//    ring slot, one barrier, one softmax step), which halves the per-page
+//    control work of the loop;
 //  * a warp serves every query head of its KV head (up to 8 per pass; the
 //    reference re-reads each KV page once per query head);
 //  * a page's K/V are dequantised in registers straight into tensor-core
@@ -47,14 +50,16 @@ template <int D>
 struct DecodeTraits {
   static constexpr int kWarps = 4;     // independent streaming warps per CTA
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kCtasPerSm = 4;   // 16 warps per SM (128 registers, 50 KB smem per CTA)
-  static constexpr int kRing = 12288;  // bytes of ring per warp
+  static constexpr int kCtasPerSm = 4;   // 16 warps per SM (128 registers, 53 KB smem per CTA)
+  static constexpr int kRing = 13312;  // bytes of ring per warp (3 INT4 page pairs)
   static constexpr int kSlots = 8;     // records in flight per warp
   static constexpr int DK = D / 4;     // K dims a lane owns per row
   static constexpr int DV = D / 8;     // V dims a lane owns per row
   static constexpr int kTiles = D / 16;
   static constexpr int kSmem = kWarps * kRing + kWarps * kSlots * (8 + 4 + 4 + 4);
   static_assert(kRing % 16 == 0 && kRing >= 4 * kBlock * D, "a ring must hold one FP16 record");
+  // Two INT8 records with the finest scale group (32) form the largest pair.
+  static_assert(kRing >= 2 * (2 * kBlock * D + 2 * (kBlock * D / 32) * 2 + 16), "a ring must hold a pair");
 };
 
 // Workspace header (int32 words), written by the decode kernel, read by merge.
@@ -269,23 +274,34 @@ struct SoftmaxState {
   float m0, m1, l0, l1;  // heads 2t4, 2t4+1: running max (base 2) and this lane's sum
 };
 
-// Online softmax of one page's scores; returns the fp16 P fragments for P.V,
-// multiplied by `pscale` (the page's V scale when it is folded into P; the
-// running sums take the unscaled P).
-template <int D>
-__device__ __forceinline__ void page_softmax(float (&s)[4], int ntok, int gid, float scale_log2,
-                                             float pscale, SoftmaxState &st, float (&o)[D / 16][4],
-                                             uint32_t &b0, uint32_t &b1) {
+// Online softmax step over one or two pages of one item (fp32, base 2).
+// Returns the fp16 P fragments for P.V, page r's multiplied by ps[r] (its V
+// scale when that is folded into P; the running sums take the unscaled P).
+// Scores are scaled before the max, so any sign of the softmax scale works.
+// The running max moves only when a score exceeds it by more than `slack`
+// (8: P <= 2^8; 0: an exact max, P <= 1).  With NP = 2 the second page is
+// skipped when `two` is false.
+template <int D, int NP>
+__device__ __forceinline__ void pages_softmax(float (&s)[NP][4], const int (&ntok)[NP], bool two,
+                                              int gid, float scale_log2, float slack,
+                                              const float (&ps)[NP], SoftmaxState &st,
+                                              float (&o)[D / 16][4], uint32_t (&b)[NP][2]) {
   constexpr float kNegInf = -INFINITY;
-  if (ntok < kBlock) {  // tokens past the page's valid count do not exist
-    if (gid >= ntok) s[0] = s[1] = kNegInf;
-    if (gid + 8 >= ntok) s[2] = s[3] = kNegInf;
+  float x[NP][4];
+  float mx0 = kNegInf, mx1 = kNegInf;
+#pragma unroll
+  for (int r = 0; r < NP; ++r) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[r][i] = s[r][i] * scale_log2;
+    if (ntok[r] < kBlock) {  // tokens past the page's valid count do not exist
+      if (gid >= ntok[r]) x[r][0] = x[r][1] = kNegInf;
+      if (gid + 8 >= ntok[r]) x[r][2] = x[r][3] = kNegInf;
+    }
+    mx0 = fmaxf(mx0, fmaxf(x[r][0], x[r][2]));
+    mx1 = fmaxf(mx1, fmaxf(x[r][1], x[r][3]));
   }
-  float mx0 = fmaxf(s[0], s[2]) * scale_log2, mx1 = fmaxf(s[1], s[3]) * scale_log2;
-  // Lazy rescale: keep the running max unless some score exceeds it by > 8
-  // (P <= 2^8 in fp16 is exact enough and cannot overflow).  Only then reduce
-  // the page max across the lanes that share a head.
-  if (__any_sync(0xffffffffu, mx0 > st.m0 + 8.f || mx1 > st.m1 + 8.f)) {
+  // Lazy rescale: only then reduce the max across the lanes sharing a head.
+  if (__any_sync(0xffffffffu, mx0 > st.m0 + slack || mx1 > st.m1 + slack)) {
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
@@ -298,52 +314,98 @@ __device__ __forceinline__ void page_softmax(float (&s)[4], int ntok, int gid, f
     for (int m = 0; m < D / 16; ++m) o[m][0] *= a0, o[m][1] *= a1, o[m][2] *= a0, o[m][3] *= a1;
     st.m0 = n0, st.m1 = n1;
   }
-  const float p0 = ex2(fmaf(s[0], scale_log2, -st.m0));
-  const float p1 = ex2(fmaf(s[1], scale_log2, -st.m1));
-  const float p2 = ex2(fmaf(s[2], scale_log2, -st.m0));
-  const float p3 = ex2(fmaf(s[3], scale_log2, -st.m1));
-  st.l0 += p0 + p2, st.l1 += p1 + p3;
-  b0 = movmatrix_trans(pack_f16x2(p0 * pscale, p1 * pscale));
-  b1 = movmatrix_trans(pack_f16x2(p2 * pscale, p3 * pscale));
+#pragma unroll
+  for (int r = 0; r < NP; ++r) {
+    if (r > 0 && !two) break;
+    const float p0 = ex2(x[r][0] - st.m0), p1 = ex2(x[r][1] - st.m1);
+    const float p2 = ex2(x[r][2] - st.m0), p3 = ex2(x[r][3] - st.m1);
+    st.l0 += p0 + p2, st.l1 += p1 + p3;
+    b[r][0] = movmatrix_trans(pack_f16x2(p0 * ps[r], p1 * ps[r]));
+    b[r][1] = movmatrix_trans(pack_f16x2(p2 * ps[r], p3 * ps[r]));
+  }
 }
 
-template <int D, int MODE, bool SLAB>
-__device__ __forceinline__ void page_attend(uint8_t *rec, int ntok, int lane, int log2_group,
-                                            const ScaleIdx &si, const uint32_t (&qf)[D / 16][2],
-                                            float scale_log2, SoftmaxState &st,
-                                            float (&o)[D / 16][4]) {
+// Zero the V rows past a partial page's valid count, so that P = 0 never meets
+// a non-finite value.
+template <int D, int MODE>
+__device__ __forceinline__ void zero_tail(uint8_t *rec, int ntok, int lane) {
   constexpr int PB = kBlock * D * mode_bits(MODE) / 8;
+  constexpr int rowB = D * mode_bits(MODE) / 8;
+  for (int off = ntok * rowB + 4 * lane; off < PB; off += 128)
+    *reinterpret_cast<uint32_t *>(rec + PB + off) = 0u;
+}
+
+// One FP16 page.
+template <int D, bool SLAB>
+__device__ __forceinline__ void fp16_attend(uint8_t *rec, int ntok, int lane,
+                                            const uint32_t (&qf)[D / 16][2], float scale_log2,
+                                            SoftmaxState &st, float (&o)[D / 16][4]) {
+  constexpr int PB = kBlock * D * 2;
   const int gid = lane >> 2, t4 = lane & 3;
   if (ntok < kBlock) {
-    // Zero the V rows past the valid count so P=0 never meets a non-finite value.
-    constexpr int rowB = D * mode_bits(MODE) / 8;
-    for (int off = ntok * rowB + 4 * lane; off < PB; off += 128)
-      *reinterpret_cast<uint32_t *>(rec + PB + off) = 0u;
+    zero_tail<D, AKV_MODE_FP16>(rec, ntok, lane);
     __syncwarp();
   }
-  const __half *ksc = reinterpret_cast<const __half *>(rec + 2 * PB);
-  const __half *vsc = ksc + (SLAB ? 1 : ((kBlock * D) >> log2_group));
-  float s[4];
-  uint32_t b0, b1;
-  if constexpr (SLAB && MODE != AKV_MODE_FP16) {
-    // One V scale per page: P.V = (P * sV) . v_int, so no V element is
-    // multiplied by its scale (the rounding moves from fp16(int * sV) to
-    // fp16(P * sV), both one fp16 rounding per term).  K keeps the reference's
-    // per-element fp16(int * sK): the scores amplify that rounding through exp.
-    // P <= 2^8 (lazy softmax), so P * sV stays finite in fp16 while sV <= 255;
-    // larger V scales (values beyond +-1785 in INT4) take the per-element path.
-    const float sv = __half2float(*vsc);
-    page_qk<D, MODE, SLAB>(rec, ksc, si, gid, t4, qf, s);
-    const bool fold_v = sv <= 255.f;
-    page_softmax<D>(s, ntok, gid, scale_log2, fold_v ? sv : 1.f, st, o, b0, b1);
-    if (fold_v)
-      page_pv<D, MODE, SLAB, true>(rec + PB, vsc, si, gid, t4, b0, b1, o);
-    else
-      page_pv<D, MODE, SLAB, false>(rec + PB, vsc, si, gid, t4, b0, b1, o);
-  } else {
-    page_qk<D, MODE, SLAB>(rec, ksc, si, gid, t4, qf, s);
-    page_softmax<D>(s, ntok, gid, scale_log2, 1.f, st, o, b0, b1);
-    page_pv<D, MODE, SLAB, false>(rec + PB, vsc, si, gid, t4, b0, b1, o);
+  const ScaleIdx none{0, 0, 0};
+  float s[1][4];
+  uint32_t b[1][2];
+  const int nt[1] = {ntok};
+  const float ps[1] = {1.f};
+  page_qk<D, AKV_MODE_FP16, SLAB>(rec, nullptr, none, gid, t4, qf, s[0]);
+  pages_softmax<D, 1>(s, nt, false, gid, scale_log2, 8.f, ps, st, o, b);
+  page_pv<D, AKV_MODE_FP16, SLAB, false>(rec + PB, nullptr, none, gid, t4, b[0][0], b[0][1], o);
+}
+
+// A slot of one or two INT8/INT4 pages of one item, adjacent in the ring
+// (`rb` bytes apart), sharing one softmax step.  The two pages run through the
+// same Q.K and P.V code (a two-trip loop keeps one copy of it per mode).
+// With one scale per page (SLAB) each page's V scale is folded into its P
+// fragment: P.V = (P * sV) . v_int, one fp16 rounding per term as in
+// fp16(int * sV).  P <= 2^8 keeps P * sV finite while sV <= 255; a slot with a
+// larger V scale takes an exact running max (P <= 1, so P * sV <= sV).  K keeps
+// the exact per-element fp16(int * sK): the scores would amplify any change
+// through exp.
+template <int D, int MODE, bool SLAB>
+__device__ __forceinline__ void slot_attend(uint8_t *rec, uint32_t rb, bool has2, int ntok0,
+                                            int ntok1, int lane, int log2_group, const ScaleIdx &si,
+                                            const uint32_t (&qf)[D / 16][2], float scale_log2,
+                                            SoftmaxState &st, float (&o)[D / 16][4]) {
+  constexpr int PB = kBlock * D * mode_bits(MODE) / 8;
+  const int gid = lane >> 2, t4 = lane & 3;
+  const int npages = has2 ? 2 : 1;
+  if (ntok0 < kBlock || (has2 && ntok1 < kBlock)) {
+    if (ntok0 < kBlock) zero_tail<D, MODE>(rec, ntok0, lane);
+    if (has2 && ntok1 < kBlock) zero_tail<D, MODE>(rec + rb, ntok1, lane);
+    __syncwarp();
+  }
+  const int vgap = SLAB ? 1 : ((kBlock * D) >> log2_group);  // K scales, then V scales
+  float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 1
+  for (int r = 0; r < npages; ++r) {
+    const uint8_t *pg = rec + r * rb;
+    float sr[4];
+    page_qk<D, MODE, SLAB>(pg, reinterpret_cast<const __half *>(pg + 2 * PB), si, gid, t4, qf, sr);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      s[0][i] = r ? s[0][i] : sr[i];
+      s[1][i] = r ? sr[i] : s[1][i];
+    }
+  }
+  const int nt[2] = {ntok0, has2 ? ntok1 : 0};
+  float ps[2] = {1.f, 1.f};
+  float slack = 8.f;
+  if constexpr (SLAB) {
+    ps[0] = __half2float(reinterpret_cast<const __half *>(rec + 2 * PB)[vgap]);
+    ps[1] = has2 ? __half2float(reinterpret_cast<const __half *>(rec + rb + 2 * PB)[vgap]) : 0.f;
+    if (!(fmaxf(ps[0], ps[1]) <= 255.f)) slack = 0.f;
+  }
+  uint32_t b[2][2];
+  pages_softmax<D, 2>(s, nt, has2, gid, scale_log2, slack, ps, st, o, b);
+#pragma unroll 1
+  for (int r = 0; r < npages; ++r) {
+    const uint8_t *pg = rec + r * rb;
+    page_pv<D, MODE, SLAB, SLAB>(pg + PB, reinterpret_cast<const __half *>(pg + 2 * PB) + vgap, si, gid, t4,
+                                 r ? b[1][0] : b[0][0], r ? b[1][1] : b[0][1], o);
   }
 }
 
@@ -449,12 +511,15 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
   };
   int64_t w_src = 0;
   uint32_t w_rb = 0, w_meta = 0, w_mask = 0;
+  uint32_t w_m4 = 0, w_m8 = 0, w_bnd = 0;  // lanes holding INT4 / INT8 pages; lanes starting an item
   auto prepare = [&](int w0, int64_t raw, int nb) {
     const int e = w0 + lane;
-    bool ok = false;
+    bool ok = false, first = false;
+    int mode = AKV_MODE_SKIP;
     if (e < e_end) {
       const int it = e / mb, j = e - it * mb;
-      const int mode = j < nb ? desc_mode(raw) : AKV_MODE_SKIP;
+      first = j == 0;
+      mode = j < nb ? desc_mode(raw) : AKV_MODE_SKIP;
       w_rb = mode == AKV_MODE_FP16 ? rb16 : (mode == AKV_MODE_INT8 ? rb8 : rb4);
       const int64_t poff = desc_offset(raw);
       ok = mode != AKV_MODE_SKIP;
@@ -466,6 +531,9 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
       w_meta = (uint32_t)mode | ((uint32_t)desc_ntok(raw) << 4) | ((uint32_t)(it - first_item) << 16);
     }
     w_mask = __ballot_sync(0xffffffffu, ok);
+    w_m4 = __ballot_sync(0xffffffffu, ok && mode == AKV_MODE_INT4);
+    w_m8 = __ballot_sync(0xffffffffu, ok && mode == AKV_MODE_INT8);
+    w_bnd = __ballot_sync(0xffffffffu, first);
   };
   int win0 = e_begin;
   int64_t nxt_raw;
@@ -547,7 +615,16 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
         continue;
       }
       const int k = __ffs(w_mask) - 1;
+      // An INT8 or INT4 page takes the next page of its item and mode in the
+      // window as its partner: one slot, one barrier and one softmax step for
+      // both.  FP16 pages go alone (two would not fit the ring).
+      const uint32_t kbit = 1u << k, higher = ~((kbit << 1) - 1u);
+      const uint32_t same = (w_m4 & kbit) ? w_m4 : ((w_m8 & kbit) ? w_m8 : 0u);
+      const uint32_t bnd = w_bnd & higher;  // first lane of the next item, if in the window
+      const uint32_t cand = same & w_mask & higher & (bnd ? (bnd & (0u - bnd)) - 1u : 0xffffffffu);
+      const int k2 = cand ? __ffs(cand) - 1 : k;
       const uint32_t rb = __shfl_sync(0xffffffffu, w_rb, k);
+      const uint32_t need = cand ? 2u * rb : rb;
       // Ring space: virtual byte counters (head, tail) grow monotonically (a
       // warp moves far less than 4 GB per launch) and measure occupancy; the
       // physical write position head_p is tracked beside them (no modulo).
@@ -556,27 +633,31 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
         start += T::kRing - start_p;
         start_p = 0;
         tail = start;
-      } else if (start_p + rb > (uint32_t)T::kRing) {  // wrap to the next lap
+      } else if (start_p + need > (uint32_t)T::kRing) {  // wrap to the next lap
         start += T::kRing - start_p;
         start_p = 0;
       }
-      if (start + rb - tail > (uint32_t)T::kRing) break;  // wait for room
+      if (start + need - tail > (uint32_t)T::kRing) break;  // wait for room
       const int64_t src = __shfl_sync(0xffffffffu, w_src, k);
+      const int64_t src2 = __shfl_sync(0xffffffffu, w_src, k2);
       const uint32_t meta = __shfl_sync(0xffffffffu, w_meta, k);
+      const uint32_t meta2 = __shfl_sync(0xffffffffu, w_meta, k2);
       const int slot = issued % T::kSlots;
       if (lane == 0) {
         slot_start[slot] = start;
         slot_phys[slot] = start_p;
-        slot_meta[slot] = meta;
-        fence_proxy_async_smem();  // prior generic reads of this space before the async write
+        slot_meta[slot] = meta | (cand ? 4u | (((meta2 >> 4) & 31u) << 9) : 0u);
+        // No proxy fence before the copy: every generic read of this ring
+        // space has returned its value (consumed by the page math) already.
         const uint32_t bar = smem_u32(&bars[slot]);
-        mbar_expect_tx(bar, rb);
+        mbar_expect_tx(bar, need);
         bulk_g2s(smem_u32(ring + start_p), p.arena + src, rb, bar);
+        if (cand) bulk_g2s(smem_u32(ring + start_p + rb), p.arena + src2, rb, bar);
       }
-      head = start + rb;
-      head_p = start_p + rb;
+      head = start + need;
+      head_p = start_p + need;
       ++issued;
-      w_mask &= w_mask - 1;
+      w_mask &= ~(kbit | (1u << k2));
     }
     __syncwarp();
     if (issued == consumed) break;
@@ -593,16 +674,17 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
       finalize(cur_seg);
       next_segment();
     }
-    const int ntok = (int)((meta >> 4) & 31);
+    const int ntok = (int)((meta >> 4) & 31), ntok1 = (int)((meta >> 9) & 31);
+    const bool has2 = (meta & 4u) != 0;
     switch (meta & 3u) {
       case AKV_MODE_INT4:
-        page_attend<D, AKV_MODE_INT4, SLAB>(rec, ntok, lane, lg, si, qf, p.scale_log2, st, o);
+        slot_attend<D, AKV_MODE_INT4, SLAB>(rec, rb4, has2, ntok, ntok1, lane, lg, si, qf, p.scale_log2, st, o);
         break;
       case AKV_MODE_INT8:
-        page_attend<D, AKV_MODE_INT8, SLAB>(rec, ntok, lane, lg, si, qf, p.scale_log2, st, o);
+        slot_attend<D, AKV_MODE_INT8, SLAB>(rec, rb8, has2, ntok, ntok1, lane, lg, si, qf, p.scale_log2, st, o);
         break;
       default:
-        page_attend<D, AKV_MODE_FP16, SLAB>(rec, ntok, lane, lg, si, qf, p.scale_log2, st, o);
+        fp16_attend<D, SLAB>(rec, ntok, lane, qf, p.scale_log2, st, o);
         break;
     }
     __syncwarp();

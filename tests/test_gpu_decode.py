@@ -110,6 +110,36 @@ def test_random_batches_against_oracle(cuda, case):
     assert akv.take_device_status(cuda) == 0
 
 
+@pytest.mark.parametrize("scale_sign,v_big", [(-1, None), (1, "all"), (1, "some")],
+                         ids=["negative_scale", "large_v_scales", "mixed_v_scales"])
+def test_scale_edge_cases_against_oracle(cuda, scale_sign, v_big):
+    """A negative softmax scale (the page max must be taken after scaling), and
+    V values beyond +-1785 whose INT4/INT8 scales exceed 255, so those pages
+    take the exact per-element path instead of folding the V scale into P."""
+    batch, hq, hkv, dim, tokens = 3, 16, 8, 128, 16 * 37 + 5
+    nblk = -(-tokens // 16)
+    k = W.outlier_kv(31, (batch, hkv, tokens, dim))
+    v = W.outlier_kv(32, (batch, hkv, tokens, dim))
+    if v_big == "all":
+        v = (v * 400).clamp(-60000, 60000)
+    elif v_big == "some":
+        v[:, :, 16 * 5:16 * 9] *= 400  # pages 5-8 of every sequence
+        v = v.clamp(-60000, 60000)
+    q = W.normal(33, (batch, hq, 1, dim))
+    bits = np.array(W.draw_modes(34, batch * nblk, {16: .1, 8: .4, 4: .5})).reshape(batch, nblk)
+    counts = {b: int((bits == b).sum()) for b in (16, 8, 4)}
+    pool = P.PagePool(hkv, dim, group=16 * dim, pages=counts, device=cuda, shuffle_seed=5)
+    store = P.pack_dense(pool, k.to(cuda), v.to(cuda), bits)
+    scale = scale_sign / math.sqrt(dim)
+    out = akv.packed_attention(q.to(cuda), store, scale, splits=4)
+    oracle = paged_decode_f64(q[:, :, 0].numpy(), k.numpy(), v.numpy(), bits, scale, group=16 * dim,
+                              semantics="tensor")
+    assert torch.isfinite(out).all()
+    norm = 400.0 if v_big else 1.0  # same tolerance relative to the V magnitude
+    _close(out.float() / norm, oracle / norm)
+    assert akv.take_device_status(cuda) == 0
+
+
 def test_fully_masked_sequence_outputs_zeros(cuda):
     k = W.outlier_kv(1, (2, 2, 64, 128))
     q = W.normal(2, (2, 4, 1, 128)).to(cuda)
