@@ -5,11 +5,13 @@ same arguments, same validation errors, output in the query's dtype and shape.
 It also accepts a :class:`~anchorkv_b200.pool.PagedBatch` (batch of sequences
 over a shared page pool), where the query is ``[batch, Hq, 1, D]``.
 
-The work runs in two sm_100a kernels behind the C ABI (akv_packed_attention):
-the paged decode (persistent stream-K: every resident warp takes a contiguous
-range of (sequence, KV head, page) work, bulk-copies the pages into a private
+The work runs in sm_100a kernels behind the C ABI (akv_packed_attention): the
+paged decode (persistent stream-K: every resident warp takes a contiguous range
+of (sequence, KV head, page) work, bulk-copies the pages into a private
 shared-memory ring, dequantises in registers into mma.sync fragments and keeps
-an fp32 online softmax) and the log-sum-exp merge of the partial states.
+an fp32 online softmax) and the log-sum-exp merge of the partial states (one
+warp per (sequence, query head), or a CTA per row for long sequences), each
+launched as a programmatic dependent of the kernel before it.
 """
 
 from __future__ import annotations

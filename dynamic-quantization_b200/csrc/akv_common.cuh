@@ -172,6 +172,16 @@ __device__ __forceinline__ uint32_t int8_to_f16x2(uint32_t w) {
   return hsub2(and_xor(w, 0x00FF00FFu, 0x64806480u), 0x64806480u);
 }
 
+// ------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while its
+// predecessor in the stream is still running; grid_dependency_wait() returns
+// once that predecessor has completed and its memory is visible, and
+// allow_dependents_launch() lets this kernel's own successor start early.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // --------------------------------------------------------- PTX: tensor cores
 // D = A(16x16, row) * B(16x8, col) + D, f16 inputs, f32 accumulation.
 __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,

@@ -65,10 +65,12 @@ struct DecodeTraits {
 // Workspace header (int32 words), written by the decode kernel, read by merge.
 enum HeaderField {
   kMagic, kWarpsF, kSmaxF, kRangeF, kMaxBlocksF, kItemsF, kKvHeadsF, kQGroupsF, kGqaF,
-  kHeadDimF, kSlotHeadsF, kQHeadsF, kBatchF, kHeaderWords
+  kHeadDimF, kSlotHeadsF, kQHeadsF, kBatchF, kPartialsF, kHeaderWords
 };
-constexpr int32_t kHeaderMagic = 0x414b5632;  // "AKV2"
+constexpr int32_t kHeaderMagic = 0x414b5633;  // "AKV3"
 constexpr int64_t kHeaderBytes = 256;
+// Workspace: the header, then the partial states (kPartialsF holds their
+// offset in 4-byte words).
 
 struct DecodeParams {
   const uint8_t *arena;
@@ -452,12 +454,20 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, t4 = lane & 3;
+  // Launched as a programmatic dependent: inputs (pages, table, queries) and the
+  // workspace (a previous merge may still read it) are touched only after the
+  // predecessor completes.  The merge that follows may launch right away; it
+  // waits for this grid in turn.
+  grid_dependency_wait();
+  allow_dependents_launch();
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     int32_t *h = p.header;
     h[kMagic] = kHeaderMagic, h[kWarpsF] = p.warps, h[kSmaxF] = p.smax, h[kRangeF] = p.range;
     h[kMaxBlocksF] = p.max_blocks, h[kItemsF] = p.items, h[kKvHeadsF] = p.kv_heads;
     h[kQGroupsF] = p.qgroups, h[kGqaF] = p.gqa, h[kHeadDimF] = D, h[kSlotHeadsF] = p.slot_heads;
     h[kQHeadsF] = p.q_heads, h[kBatchF] = p.batch;
+    h[kPartialsF] = (int32_t)((reinterpret_cast<const uint8_t *>(p.partials) -
+                               reinterpret_cast<const uint8_t *>(p.header)) / 4);
   }
   const int gw = blockIdx.x * T::kWarps + warp;
   const int mb = p.max_blocks;
@@ -705,69 +715,165 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
   }
 }
 
-// Merge the partial states of the warps that touched each (sequence, query
-// head).  One CTA of 4 warps per (query head, sequence): warp w folds
-// contributors w, w+4, ... with a single-pass online LSE merge (each lane owns
-// D/32 dims, loaded as one vector), then the 4 warps combine in shared memory.
-// A long single sequence has hundreds of contributors per head; a batch has
-// two or three.
+// The decomposition a merge reads back from the workspace header (the first
+// 64 bytes, one vector load each for 16 lanes' worth of fields).
+struct MergeGeom {
+  const float *partials;
+  int warps, smax, range, mb, kv_heads, qgroups, gqa, slot_heads;
+};
 template <int D>
-__global__ void __launch_bounds__(128) merge_kernel(const int32_t *__restrict__ header,
-                                                    const float *__restrict__ partials,
-                                                    __half *__restrict__ out, int64_t obs, int64_t ohs,
-                                                    float *__restrict__ state, int32_t *status) {
-  constexpr int PS = D + 4, VEC = D / 32, RS = D + 2;
-  __shared__ float sm_acc[4][D];
-  __shared__ float sm_m[4], sm_l[4];
-  if (header[kMagic] != kHeaderMagic || header[kHeadDimF] != D) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+__device__ __forceinline__ bool merge_geom(const int32_t *header, MergeGeom &g) {
+  const int4 *hv = reinterpret_cast<const int4 *>(header);
+  const int4 a = __ldcg(hv), b = __ldcg(hv + 1), c = __ldcg(hv + 2), d = __ldcg(hv + 3);
+  const int f[16] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w, c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+  static_assert(kHeaderWords <= 16, "header fields fit one 64-byte read");
+  g.partials = reinterpret_cast<const float *>(header + f[kPartialsF]);
+  g.warps = f[kWarpsF], g.smax = f[kSmaxF], g.range = f[kRangeF], g.mb = f[kMaxBlocksF];
+  g.kv_heads = f[kKvHeadsF], g.qgroups = f[kQGroupsF], g.gqa = f[kGqaF], g.slot_heads = f[kSlotHeadsF];
+  return f[kMagic] == kHeaderMagic && f[kHeadDimF] == D;
+}
+
+// Write one merged row: the normalised fp16 output and/or the (acc, m, l) state.
+template <int D>
+__device__ __forceinline__ void store_row(int lane, int b, int h, int q_heads, float m, float l,
+                                          const float (&acc)[D / 32], __half *out, int64_t obs, int64_t ohs,
+                                          float *state) {
+  constexpr int VEC = D / 32, RS = D + 2;
+  if (out) {
+    __half *o = out + (int64_t)b * obs + (int64_t)h * ohs + VEC * lane;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) o[i] = __float2half_rn(acc[i] * inv);
+  }
+  if (state) {
+    float *st = state + ((int64_t)b * q_heads + h) * RS;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) st[VEC * lane + i] = acc[i];
+    if (lane == 0) st[D] = m, st[D + 1] = l;
+  }
+}
+
+// Merge the partial states of the warps that touched each (sequence, query
+// head) row, the online log-sum-exp of triton_decode._merge_parts
+// (triton_decode.py:70-82).  One warp per row (a batch: each (sequence, KV
+// head) spans a few warps): the row's contributors are loaded 8 at a time, so a
+// row costs one L2 round trip per 8 contributors; each lane owns D/32 dims.
+// Flattened work indices fit 31 bits (the plan checks), so int arithmetic.
+template <int D>
+__global__ void __launch_bounds__(128) merge_rows_kernel(const int32_t *__restrict__ header, int batch,
+                                                         int q_heads, __half *__restrict__ out, int64_t obs,
+                                                         int64_t ohs, float *__restrict__ state,
+                                                         int32_t *status) {
+  constexpr int PS = D + 4, VEC = D / 32, CB = 8;
+  grid_dependency_wait();  // the decode grid that wrote the workspace has completed
+  allow_dependents_launch();
+  MergeGeom g;
+  if (!merge_geom<D>(header, g)) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
     return;
   }
-  const int warps = header[kWarpsF], smax = header[kSmaxF], range = header[kRangeF];
-  const int mb = header[kMaxBlocksF], kv_heads = header[kKvHeadsF], qgroups = header[kQGroupsF];
-  const int gqa = header[kGqaF], slot_heads = header[kSlotHeadsF];
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kvh = h / gqa, r = h - kvh * gqa, qg = r >> 3, n = r & 7;
-  const int64_t item = ((int64_t)b * kv_heads + kvh) * qgroups + qg;
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= batch * q_heads) return;
+  const int b = row / q_heads, h = row - b * q_heads;
+  const int kvh = h / g.gqa, r = h - kvh * g.gqa, qg = r >> 3, n = r & 7;
+  const int item = (b * g.kv_heads + kvh) * g.qgroups + qg;
   float m = -INFINITY, l = 0.f, acc[VEC];
 #pragma unroll
   for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
-  if (mb > 0) {
-    const int64_t w0 = item * mb / range;
-    const int64_t w1 = min(((item + 1) * mb - 1) / range, (int64_t)warps - 1);
-    int64_t w = w0 + warp;
+  if (g.mb > 0) {
+    const int w0 = item * g.mb / g.range;
+    const int nc = min(((item + 1) * g.mb - 1) / g.range, g.warps - 1) - w0 + 1;
+    int e = w0 * g.range, fi = e / g.mb;  // first entry of warp w0 + c, and its item
+    e -= fi * g.mb;                       // ... as an offset into that item
+    for (int c0 = 0; c0 < nc; c0 += CB) {
+      float mw[CB], lw[CB], a[CB][VEC];
+#pragma unroll
+      for (int j = 0; j < CB; ++j) {
+        mw[j] = -INFINITY;
+        if (c0 + j < nc) {
+          const int w = w0 + c0 + j;
+          const float *pr = g.partials + ((int64_t)(w * g.smax + (item - fi)) * g.slot_heads + n) * PS;
+          e += g.range;  // advance to warp w + 1
+          while (e >= g.mb) e -= g.mb, ++fi;
+          mw[j] = __ldcg(pr + D), lw[j] = __ldcg(pr + D + 1);
+          if constexpr (VEC == 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(pr) + lane);
+            a[j][0] = v.x, a[j][1] = v.y, a[j][2] = v.z, a[j][3] = v.w;
+          } else {
+            const float2 v = __ldcg(reinterpret_cast<const float2 *>(pr) + lane);
+            a[j][0] = v.x, a[j][1] = v.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < CB; ++j) {
+        if (mw[j] == -INFINITY) continue;  // an empty share weighs 0 (triton_decode.py:78)
+        const float top = fmaxf(m, mw[j]);
+        const float c = ex2(m - top), e2 = ex2(mw[j] - top);
+        l = l * c + e2 * lw[j];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * c + e2 * a[j][i];
+        m = top;
+      }
+    }
+  }
+  store_row<D>(lane, b, h, q_heads, m, l, acc, out, obs, ohs, state);
+}
+
+// The same merge for rows with hundreds of contributors (a long single
+// sequence): one CTA of 32 warps per row, warp w folds contributors w, w+32, ...
+// and the warps combine in shared memory.
+template <int D>
+__global__ void __launch_bounds__(1024) merge_wide_kernel(const int32_t *__restrict__ header, int q_heads,
+                                                          __half *__restrict__ out, int64_t obs, int64_t ohs,
+                                                          float *__restrict__ state, int32_t *status) {
+  constexpr int PS = D + 4, VEC = D / 32, W = 32;
+  __shared__ float sm_acc[W][D];
+  __shared__ float sm_m[W], sm_l[W];
+  grid_dependency_wait();
+  allow_dependents_launch();
+  MergeGeom g;
+  if (!merge_geom<D>(header, g)) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+    return;
+  }
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = h / g.gqa, r = h - kvh * g.gqa, qg = r >> 3, n = r & 7;
+  const int item = (b * g.kv_heads + kvh) * g.qgroups + qg;
+  float m = -INFINITY, l = 0.f, acc[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
+  if (g.mb > 0) {
+    const int w0 = item * g.mb / g.range;
+    const int w1 = min(((item + 1) * g.mb - 1) / g.range, g.warps - 1);
+    int w = w0 + warp;
     if (w <= w1) {
-      // first item of contributor w, advanced incrementally by 4 contributors
-      int64_t first = w * range / mb, rem = w * range - first * mb;
-      const int64_t stride = 4ll * range, sq = stride / mb, sr = stride - sq * mb;
+      // first item of contributor w, advanced incrementally by W contributors
+      int first = w * g.range / g.mb, rem = w * g.range - first * g.mb;
+      const int stride = W * g.range, sq = stride / g.mb, sr = stride - sq * g.mb;
 #pragma unroll 2
-      for (; w <= w1; w += 4) {
-        const float *pr = partials + ((w * smax + (item - first)) * slot_heads + n) * PS;
-        const float mw = pr[D], lw = pr[D + 1];
+      for (; w <= w1; w += W) {
+        const float *pr = g.partials + ((int64_t)(w * g.smax + (item - first)) * g.slot_heads + n) * PS;
+        const float mw = __ldcg(pr + D), lw = __ldcg(pr + D + 1);
         float a[VEC];
         if constexpr (VEC == 4) {
-          const float4 v = *reinterpret_cast<const float4 *>(pr + 4 * lane);
+          const float4 v = __ldcg(reinterpret_cast<const float4 *>(pr) + lane);
           a[0] = v.x, a[1] = v.y, a[2] = v.z, a[3] = v.w;
         } else {
-          const float2 v = *reinterpret_cast<const float2 *>(pr + 2 * lane);
+          const float2 v = __ldcg(reinterpret_cast<const float2 *>(pr) + lane);
           a[0] = v.x, a[1] = v.y;
         }
         if (mw != -INFINITY) {  // an empty share weighs 0 (triton_decode.py:78)
-          if (mw > m) {
-            const float c = ex2(m - mw);
-            l *= c;
+          const float top = fmaxf(m, mw);
+          const float c = ex2(m - top), e = ex2(mw - top);
+          l = l * c + e * lw;
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) acc[i] *= c;
-            m = mw;
-          }
-          const float e = ex2(mw - m);
-          l += e * lw;
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) acc[i] += e * a[i];
+          for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * c + e * a[i];
+          m = top;
         }
         first += sq, rem += sr;
-        if (rem >= mb) rem -= mb, ++first;
+        if (rem >= g.mb) rem -= g.mb, ++first;
       }
     }
   }
@@ -775,24 +881,21 @@ __global__ void __launch_bounds__(128) merge_kernel(const int32_t *__restrict__ 
   for (int i = 0; i < VEC; ++i) sm_acc[warp][VEC * lane + i] = acc[i];
   if (lane == 0) sm_m[warp] = m, sm_l[warp] = l;
   __syncthreads();
-  const int d = threadIdx.x;
-  if (d < D) {
+  if (warp == 0) {
     float top = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) top = fmaxf(top, sm_m[k]);
-    float num = 0.f, den = 0.f;
+    for (int k = 0; k < W; ++k) top = fmaxf(top, sm_m[k]);
+    float num[VEC], den = 0.f;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int i = 0; i < VEC; ++i) num[i] = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < W; ++k) {
       const float e = sm_m[k] == -INFINITY ? 0.f : ex2(sm_m[k] - top);
-      num += e * sm_acc[k][d];
       den += e * sm_l[k];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) num[i] += e * sm_acc[k][VEC * lane + i];
     }
-    if (out) out[(int64_t)b * obs + (int64_t)h * ohs + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
-    if (state) {
-      float *st = state + ((int64_t)b * gridDim.x + h) * RS;
-      st[d] = num;
-      if (d == 0) st[D] = top, st[D + 1] = den;
-    }
+    store_row<D>(lane, b, h, q_heads, top, den, num, out, obs, ohs, state);
   }
 }
 
@@ -894,13 +997,32 @@ extern "C" int64_t akv_workspace_bytes(int batch, int q_heads, int kv_heads, int
   return pl.bytes;
 }
 
-extern "C" int akv_decode_partials(const void *arena, int64_t arena_bytes, const int64_t *table,
-                                   int64_t table_stride, const int32_t *seq_blocks,
-                                   int32_t max_blocks, const void *query, int64_t q_batch_stride,
-                                   int64_t q_head_stride, int32_t batch, int32_t q_heads,
-                                   int32_t kv_heads, int32_t head_dim, int32_t group, float scale,
-                                   int32_t splits, void *workspace, int64_t workspace_bytes,
-                                   int32_t *dev_status, void *stream) {
+namespace akv {
+// Launch with programmatic stream serialization: the kernel may begin while its
+// predecessor in the stream finishes (it calls grid_dependency_wait() before
+// touching memory the predecessor may write or read).
+template <typename... Params, typename... Args>
+static cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                                    cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// Validate, plan and launch the decode kernel.
+static int decode_launch(const void *arena, int64_t arena_bytes, const int64_t *table, int64_t table_stride,
+                         const int32_t *seq_blocks, int32_t max_blocks, const void *query,
+                         int64_t q_batch_stride, int64_t q_head_stride, int32_t batch, int32_t q_heads,
+                         int32_t kv_heads, int32_t head_dim, int32_t group, float scale, int32_t splits,
+                         void *workspace, int64_t workspace_bytes, int32_t *dev_status, cudaStream_t s) {
   if (!arena || !table || !query || !workspace) return AKV_ERR_INVALID;
   if (table_stride < max_blocks || arena_bytes < 0 || !isfinite(scale)) return AKV_ERR_INVALID;
   if (((uintptr_t)arena & 15) || ((uintptr_t)query & 15) || ((uintptr_t)workspace & 15))
@@ -936,35 +1058,59 @@ extern "C" int akv_decode_partials(const void *arena, int64_t arena_bytes, const
   p.header = (int32_t *)workspace;
   p.partials = (float *)((uint8_t *)workspace + kHeaderBytes);
   p.status = dev_status;
-  cudaStream_t s = (cudaStream_t)stream;
   const bool slab = group == 16 * head_dim;
-  if (head_dim == 64) {
-    if (slab) decode_streamk_kernel<64, true><<<pl.ctas, DecodeTraits<64>::kThreads, DecodeTraits<64>::kSmem, s>>>(p);
-    else decode_streamk_kernel<64, false><<<pl.ctas, DecodeTraits<64>::kThreads, DecodeTraits<64>::kSmem, s>>>(p);
-  } else {
-    if (slab) decode_streamk_kernel<128, true><<<pl.ctas, DecodeTraits<128>::kThreads, DecodeTraits<128>::kSmem, s>>>(p);
-    else decode_streamk_kernel<128, false><<<pl.ctas, DecodeTraits<128>::kThreads, DecodeTraits<128>::kSmem, s>>>(p);
-  }
-  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+  cudaError_t err;
+  if (head_dim == 64)
+    err = launch_dependent(slab ? decode_streamk_kernel<64, true> : decode_streamk_kernel<64, false>, pl.ctas,
+                           DecodeTraits<64>::kThreads, DecodeTraits<64>::kSmem, s, p);
+  else
+    err = launch_dependent(slab ? decode_streamk_kernel<128, true> : decode_streamk_kernel<128, false>, pl.ctas,
+                           DecodeTraits<128>::kThreads, DecodeTraits<128>::kSmem, s, p);
+  return err == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+}
+
+// Merge launch.  The decode spreads all resident warps over the items, so few
+// (sequence, head) rows mean many contributors per row (a long sequence: one
+// CTA of 32 warps per row), many rows few contributors (one warp per row).
+template <int D>
+static cudaError_t merge_launch(const int32_t *header, int batch, int q_heads, __half *out, int64_t obs,
+                                int64_t ohs, float *state, int32_t *status, cudaStream_t s) {
+  const int rows = batch * q_heads;
+  if (rows < 2 * 148)
+    return launch_dependent(merge_wide_kernel<D>, dim3(q_heads, batch), 1024, 0, s, header, q_heads, out, obs,
+                            ohs, state, status);
+  return launch_dependent(merge_rows_kernel<D>, dim3((rows + 3) / 4), 128, 0, s, header, batch, q_heads, out,
+                          obs, ohs, state, status);
+}
+}  // namespace akv
+
+extern "C" int akv_decode_partials(const void *arena, int64_t arena_bytes, const int64_t *table,
+                                   int64_t table_stride, const int32_t *seq_blocks,
+                                   int32_t max_blocks, const void *query, int64_t q_batch_stride,
+                                   int64_t q_head_stride, int32_t batch, int32_t q_heads,
+                                   int32_t kv_heads, int32_t head_dim, int32_t group, float scale,
+                                   int32_t splits, void *workspace, int64_t workspace_bytes,
+                                   int32_t *dev_status, void *stream) {
+  return decode_launch(arena, arena_bytes, table, table_stride, seq_blocks, max_blocks, query, q_batch_stride,
+                       q_head_stride, batch, q_heads, kv_heads, head_dim, group, scale, splits, workspace,
+                       workspace_bytes, dev_status, (cudaStream_t)stream);
 }
 
 extern "C" int akv_merge(const void *workspace, int32_t batch, int32_t q_heads, int32_t head_dim,
                          void *out, int64_t out_batch_stride, int64_t out_head_stride,
                          float *state_out, int32_t *dev_status, void *stream) {
   if (!workspace || (!out && !state_out)) return AKV_ERR_INVALID;
-  if (batch <= 0 || q_heads <= 0 || batch > 65535) return AKV_ERR_INVALID;
+  if (batch <= 0 || q_heads <= 0 || batch > 65535 || (int64_t)batch * q_heads >= (1ll << 31))
+    return AKV_ERR_INVALID;
   if (head_dim != 64 && head_dim != 128) return AKV_ERR_UNSUPPORTED;
   const int32_t *header = (const int32_t *)workspace;
-  const float *partials = (const float *)((const uint8_t *)workspace + kHeaderBytes);
-  const dim3 grid(q_heads, batch);
   cudaStream_t s = (cudaStream_t)stream;
-  if (head_dim == 64)
-    merge_kernel<64><<<grid, 128, 0, s>>>(header, partials, (__half *)out, out_batch_stride,
-                                          out_head_stride, state_out, dev_status);
-  else
-    merge_kernel<128><<<grid, 128, 0, s>>>(header, partials, (__half *)out, out_batch_stride,
-                                           out_head_stride, state_out, dev_status);
-  return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+  const cudaError_t err =
+      head_dim == 64 ? merge_launch<64>(header, batch, q_heads, (__half *)out, out_batch_stride, out_head_stride,
+                                        state_out, dev_status, s)
+                     : merge_launch<128>(header, batch, q_heads, (__half *)out, out_batch_stride,
+                                         out_head_stride, state_out, dev_status, s);
+  return err == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
 }
 
 extern "C" int akv_merge_states(const float *states, int32_t n, int32_t batch, int32_t q_heads,
@@ -992,9 +1138,10 @@ extern "C" int akv_packed_attention(const void *arena, int64_t arena_bytes, cons
                                     int64_t out_head_stride, void *workspace,
                                     int64_t workspace_bytes, int32_t *dev_status, void *stream) {
   if (!out) return AKV_ERR_INVALID;
-  int st = akv_decode_partials(arena, arena_bytes, table, table_stride, seq_blocks, max_blocks, query,
-                               q_batch_stride, q_head_stride, batch, q_heads, kv_heads, head_dim,
-                               group, scale, splits, workspace, workspace_bytes, dev_status, stream);
+  if (batch > 65535) return AKV_ERR_INVALID;
+  const int st = akv_decode_partials(arena, arena_bytes, table, table_stride, seq_blocks, max_blocks, query,
+                                     q_batch_stride, q_head_stride, batch, q_heads, kv_heads, head_dim, group,
+                                     scale, splits, workspace, workspace_bytes, dev_status, stream);
   if (st != AKV_OK) return st;
   return akv_merge(workspace, batch, q_heads, head_dim, out, out_batch_stride, out_head_stride,
                    nullptr, dev_status, stream);

@@ -116,7 +116,8 @@ int akv_unpack_pages(const int64_t *desc, int64_t n_pages, const void *arena,
  * this geometry on the current device (-1 for invalid or unsupported arguments).
  * The workspace holds a 256-byte header describing the work decomposition and
  * one partial state (acc[head_dim], m, l) per (warp, item it touched, query
- * head); it is opaque to the caller. */
+ * head); it is opaque to the caller and needs no initialisation.  Calls that
+ * use one workspace must be ordered (one stream, or events between streams). */
 int64_t akv_workspace_bytes(int batch, int q_heads, int kv_heads, int head_dim, int max_blocks,
                             int splits);
 
@@ -157,8 +158,10 @@ int akv_merge_states(const float *states, int32_t n, int32_t batch, int32_t q_he
                      int64_t out_head_stride, void *stream);
 
 /* akv_decode_partials followed by akv_merge, partials in the caller's workspace
- * (at least akv_workspace_bytes bytes, 16-byte aligned).
- * Replaces triton_decode.packed_attention (triton_decode.py:85-104). */
+ * (at least akv_workspace_bytes bytes, 16-byte aligned).  Both kernels are
+ * launched as programmatic dependents of their predecessor in the stream, so
+ * each starts while the previous one finishes (it waits for it before touching
+ * memory).  Replaces triton_decode.packed_attention (triton_decode.py:85-104). */
 int akv_packed_attention(const void *arena, int64_t arena_bytes, const int64_t *table,
                          int64_t table_stride, const int32_t *seq_blocks, int32_t max_blocks,
                          const void *query, int64_t q_batch_stride, int64_t q_head_stride,

@@ -13,6 +13,7 @@ import torch
 
 import anchorkv_b200 as akv
 import workloads as W
+from anchorkv_b200 import _lib
 from anchorkv_b200 import pool as P
 from paged_reference import paged_decode_f64
 
@@ -114,8 +115,8 @@ def test_random_batches_against_oracle(cuda, case):
                          ids=["negative_scale", "large_v_scales", "mixed_v_scales"])
 def test_scale_edge_cases_against_oracle(cuda, scale_sign, v_big):
     """A negative softmax scale (the page max must be taken after scaling), and
-    V values beyond +-1785 whose INT4/INT8 scales exceed 255, so those pages
-    take the exact per-element path instead of folding the V scale into P."""
+    V values beyond +-1785 whose INT4/INT8 scales exceed 255: P times such a
+    scale stays finite only under an exact running max (P <= 1)."""
     batch, hq, hkv, dim, tokens = 3, 16, 8, 128, 16 * 37 + 5
     nblk = -(-tokens // 16)
     k = W.outlier_kv(31, (batch, hkv, tokens, dim))
@@ -190,3 +191,77 @@ def test_out_of_arena_descriptor_is_skipped_and_reported(cuda):
     assert akv.take_device_status(cuda) & 1
     torch.testing.assert_close(bad, expect)
     assert not torch.equal(good, expect)
+
+
+def _batch_store(cuda, batch, tokens, hq=16, hkv=8, dim=128, seed=41):
+    nblk = -(-tokens // 16)
+    k = W.outlier_kv(seed, (batch, hkv, tokens, dim))
+    v = W.outlier_kv(seed + 1, (batch, hkv, tokens, dim))
+    q = W.normal(seed + 2, (batch, hq, 1, dim))
+    bits = np.array(W.draw_modes(seed + 3, batch * nblk, {16: .15, 8: .35, 4: .4, 0: .1})).reshape(batch, nblk)
+    counts = {b: int((bits == b).sum()) for b in (16, 8, 4)}
+    pool = P.PagePool(hkv, dim, group=16 * dim, pages=counts, device=cuda, shuffle_seed=seed)
+    store = P.pack_dense(pool, k.to(cuda), v.to(cuda), bits)
+    return store, q, k, v, bits
+
+
+def _c_attention(store, q, scale, splits, ws, out, status):
+    """akv_packed_attention through the C ABI with a caller-owned workspace."""
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    B, Hq, _, D = q.shape
+    return lib.akv_packed_attention(store.pool.arena.data_ptr(), store.pool.nbytes, store.table.data_ptr(),
+                                    store.table.stride(0), store.seq_blocks.data_ptr(), store.max_blocks,
+                                    q.data_ptr(), q.stride(0), q.stride(1), B, Hq, store.heads, D, store.group,
+                                    scale, splits, out.data_ptr(), out.stride(0), out.stride(1), ws.data_ptr(),
+                                    ws.numel(), status.data_ptr(), stream)
+
+
+@pytest.mark.parametrize("batch,tokens,splits", [(24, 16 * 64, 8), (20, 16 * 200 + 7, 4), (64, 16 * 32, 0)])
+def test_row_merge_outputs_and_states_against_oracle(cuda, batch, tokens, splits):
+    """Many (sequence, query head) rows: the one-warp-per-row merge, into the
+    output and into LSE states (whose own merge gives the same output)."""
+    store, q, k, v, bits = _batch_store(cuda, batch, tokens)
+    qd = q.to(cuda)
+    assert batch * q.shape[1] >= 2 * 148  # the row merge
+    out = akv.packed_attention(qd, store, 0.088, splits=splits)
+    oracle = paged_decode_f64(q[:, :, 0].numpy(), k.numpy(), v.numpy(), bits, 0.088, group=16 * 128)
+    _close(out, oracle)
+    states = akv.decode_partial_states(qd, store, 0.088, splits=splits)
+    torch.testing.assert_close(akv.merge_states(states[None]), out, atol=1e-3, rtol=1e-3)
+    assert akv.take_device_status(cuda) == 0
+
+
+def test_long_sequence_wide_merge_against_oracle(cuda):
+    """Hundreds of warps per (sequence, KV head): a CTA of 32 warps per row."""
+    store, q, k, v, bits = _batch_store(cuda, 1, 16 * 3000, hq=32, seed=51)
+    out = akv.packed_attention(q.to(cuda), store, 0.088, splits=0)
+    oracle = paged_decode_f64(q[:, :, 0].numpy(), k.numpy(), v.numpy(), bits, 0.088, group=2048)
+    _close(out, oracle)
+    assert akv.take_device_status(cuda) == 0
+
+
+def test_workspace_needs_no_initialisation_and_survives_geometry_changes(cuda):
+    """Any bytes in the workspace, and partials of other geometries left in it,
+    do not change a result: each decode rewrites the header and every partial
+    the merge reads."""
+    lib = _lib.load()
+    status = _lib.status_word(cuda)
+    small, q_s, *_ = _batch_store(cuda, 2, 16 * 40, seed=61)
+    big, q_b, *_ = _batch_store(cuda, 24, 16 * 40, seed=71)
+    qs, qb = q_s.to(cuda), q_b.to(cuda)
+    nbytes = max(lib.akv_workspace_bytes(24, 16, 8, 128, big.max_blocks, 8),
+                 lib.akv_workspace_bytes(2, 16, 8, 128, small.max_blocks, 8))
+    clean = torch.zeros(nbytes, dtype=torch.uint8, device=cuda)
+    ref_s, ref_b = torch.empty_like(qs), torch.empty_like(qb)
+    assert _c_attention(small, qs, 0.088, 8, clean, ref_s, status) == 0
+    assert _c_attention(big, qb, 0.088, 8, clean, ref_b, status) == 0
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    for fill in ("ones", "random"):
+        ws = (torch.full((nbytes,), 255, dtype=torch.uint8, device=cuda) if fill == "ones" else
+              torch.randint(0, 256, (nbytes,), generator=gen, dtype=torch.uint8, device=cuda))
+        for store, qq, ref in ((small, qs, ref_s), (big, qb, ref_b), (small, qs, ref_s)):
+            out = torch.empty_like(qq)
+            assert _c_attention(store, qq, 0.088, 8, ws, out, status) == 0
+            assert torch.equal(out, ref)
+    assert akv.take_device_status(cuda) == 0
