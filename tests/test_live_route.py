@@ -1,0 +1,77 @@
+"""Hugging Face integration (colab_experiment.py:86-155, 294-313 of the reference):
+the attention route and live cache, with the reference's model gate as parity.
+
+No checkpoint is available offline, so the models are randomly initialised
+Qwen3 architectures (fp16 on the GPU); the gate compares two attention
+implementations over the same stores, which holds for any weights."""
+
+import pytest
+import torch
+
+from anchorkv_b200 import live
+
+
+def _qwen3(head_dim, heads, kv_heads, layers, device, dtype, seed=0):
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    torch.manual_seed(seed)
+    config = Qwen3Config(vocab_size=2048, hidden_size=heads * head_dim, intermediate_size=2 * heads * head_dim,
+                         num_hidden_layers=layers, num_attention_heads=heads, num_key_value_heads=kv_heads,
+                         head_dim=head_dim, max_position_embeddings=4096, attn_implementation="sdpa")
+    return Qwen3ForCausalLM(config).to(device=device, dtype=dtype).eval()
+
+
+@torch.inference_mode()
+def test_route_without_cache_captures_queries_and_restores_registry():
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+
+    model = _qwen3(32, 4, 2, 2, "cpu", torch.float32)
+    ids = torch.randint(0, 2048, (1, 21), generator=torch.Generator().manual_seed(1))
+    prefill = model(input_ids=ids[:, :-1], use_cache=True, logits_to_keep=1)
+    source = live.cache_cpu(prefill.past_key_values)
+    assert len(source) == 2 and source[0][0].shape == (1, 2, 20, 32)
+    stock = model(input_ids=ids[:, -1:], past_key_values=live.stock_cache(source, "cpu"), use_cache=True,
+                  logits_to_keep=1).logits
+    captured = {}
+    with live.attention_route(model, capture=captured):
+        assert model.config._attn_implementation == live.ROUTE
+        routed = live.forward_token(model, live.stock_cache(source, "cpu"), int(ids[0, -1])).logits
+    assert model.config._attn_implementation == "sdpa"
+    assert ALL_ATTENTION_FUNCTIONS[live.ROUTE] is ALL_ATTENTION_FUNCTIONS["sdpa"]
+    assert sorted(captured) == [0, 1] and captured[0].shape == (1, 4, 1, 32)
+    torch.testing.assert_close(routed, stock)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("head_dim,heads,kv_heads", [(128, 16, 8), (64, 8, 2)])
+def test_model_gate_on_random_qwen3(cuda, head_dim, heads, kv_heads):
+    """Packed route vs dense route (mean KL <= 0.002) for FP16 / INT8 / INT4
+    stores and an INT4 store with protected pages; FP16 paged vs stock."""
+    model = _qwen3(head_dim, heads, kv_heads, 4, cuda, torch.float16)
+    ids = torch.randint(0, 2048, (1, 181), generator=torch.Generator().manual_seed(2))
+    with torch.inference_mode():
+        prefill = model(input_ids=ids[:, :-1].to(cuda), use_cache=True, logits_to_keep=1)
+    source = live.cache_cpu(prefill.past_key_values)
+    forced = torch.randint(0, 2048, (8,), generator=torch.Generator().manual_seed(3)).tolist()
+    checks = live.model_gate(model, source, int(ids[0, -1]), forced, live.Settings())
+    assert [c["policy"] for c in checks] == ["paged_fp16", "int8", "int4", "oracle"]
+    assert all(c["mean_kl_dense_vs_packed"] <= 0.002 for c in checks)
+
+
+@pytest.mark.gpu
+def test_live_cache_appends_and_demotes_during_decode(cuda):
+    model = _qwen3(128, 16, 8, 2, cuda, torch.float16)
+    ids = torch.randint(0, 2048, (1, 100), generator=torch.Generator().manual_seed(4))
+    with torch.inference_mode():
+        prefill = model(input_ids=ids[:, :-1].to(cuda), use_cache=True, logits_to_keep=1)
+        source = live.cache_cpu(prefill.past_key_values)
+        cache = live.make_live_cache(source, live.Settings(), bits=4, device=cuda)
+        before = cache.report()
+        with live.attention_route(model, cache=cache, backend="packed"):
+            token = int(ids[0, -1])
+            for _ in range(40):
+                token = int(live.forward_token(model, cache, token, packed=True).logits[0, -1].argmax())
+    after = cache.report()
+    assert after["tokens"] == before["tokens"] + 40 == 139
+    assert after["demotions"] > before["demotions"]
+    assert after["payload_bytes"] < 2 * 2 * 2 * 8 * 139 * 128  # below the FP16 size of two layers' K and V
