@@ -50,6 +50,14 @@ WORKLOADS = {
     # One layer of the same step (916 MB of KV, > L2; under 1 GB on the device):
     # the case full ncu captures are taken on, its launches identical to the
     # step's.
+    # 36 layers x 128 sequences x 32,768 tokens, 32 query / 8 KV heads (GQA 4),
+    # INT4-heavy: 220 GB of KV per step, sequences sharded across the GPUs
+    # (strong scaling, no collective).  Layers cycle over as many distinct
+    # stores as fit a GPU; every launch still streams its whole store from HBM.
+    "large": dict(
+        name="large-batch decode, Qwen3-8B-like attention shape (GQA 4)",
+        layers=36, q_heads=32, kv_heads=8, dim=128, batch=128, tokens=32768,
+        mix={16: 0.095, 8: 0.19, 4: 0.665, 0: 0.05}, splits=8, group=2048, strong=True, outliers=True),
     "batched_small": dict(
         name="batched decode, Qwen3-0.6B attention shape, 1 layer (profiling case)",
         layers=1, q_heads=16, kv_heads=8, dim=128, batch=64, tokens=8192,
@@ -172,33 +180,63 @@ def cpu_baseline(wl: dict, seed: int, seconds: float, calls_min: int = 3):
 
 
 # ------------------------------------------------------------------ GPU setup
-def build_workload(wl: dict, device, seed: int):
+# Device bytes the KV stores of one GPU may take (the rest holds the fp16
+# staging of one layer, queries and workspaces).
+STORE_BUDGET = 120e9
+
+
+def layer_store_bytes(wl: dict, batch: int) -> float:
+    """Expected arena bytes of one layer's store at the workload's precision mix."""
+    from anchorkv_b200 import pool as P
+
+    pages = batch * (wl["tokens"] // 16)
+    per_page = sum(p * P.record_bytes(wl["dim"], wl["group"], b) * wl["kv_heads"]
+                   for b, p in wl["mix"].items() if b)
+    return pages * per_page
+
+
+def build_workload(wl: dict, device, seed: int, batch: int | None = None, distinct: int | None = None):
+    """Packed stores for ``distinct`` layers (all of them by default) of ``batch``
+    sequences each; layer l of the step uses store l % distinct.  Returns
+    (pool, stores per layer, queries [L, batch, Hq, 1, D], KV bytes per layer)."""
     import numpy as np
     import torch
 
     from anchorkv_b200 import pool as P
 
+    batch = wl["batch"] if batch is None else batch
+    distinct = wl["layers"] if distinct is None else distinct
     rng = np.random.default_rng(seed)
     nblk = wl["tokens"] // 16
     keys = list(wl["mix"])
     probs = np.array([wl["mix"][k] for k in keys])
-    bits = [rng.choice(np.array(keys), size=(wl["batch"], nblk), p=probs) for _ in range(wl["layers"])]
+    bits = [rng.choice(np.array(keys), size=(batch, nblk), p=probs) for _ in range(distinct)]
     counts = {b: int(sum((x == b).sum() for x in bits)) for b in (16, 8, 4)}
     pool = P.PagePool(wl["kv_heads"], wl["dim"], group=wl["group"], pages=counts, device=device,
                       shuffle_seed=seed, zero=False)
     gen = torch.Generator(device=device).manual_seed(seed)
-    shape = (wl["batch"], wl["kv_heads"], wl["tokens"], wl["dim"])
+    shape = (batch, wl["kv_heads"], wl["tokens"], wl["dim"])
     k = torch.empty(shape, dtype=torch.float16, device=device)
     v = torch.empty_like(k)
-    layers = []
+
+    def outliers(x):  # 4 channels per (sequence, head) scaled by +-8
+        ch = torch.randint(0, wl["dim"], shape[:2] + (4,), generator=gen, device=device)
+        sign = torch.where(torch.rand(shape[:2] + (4,), generator=gen, device=device) < 0.5, -8.0, 8.0)
+        x.mul_(torch.ones(shape[:2] + (wl["dim"],), device=device).scatter_(2, ch, sign).half()[:, :, None, :])
+
+    stores = []
     for layer_bits in bits:
         k.normal_(generator=gen)
         v.normal_(generator=gen)
-        layers.append(P.pack_dense(pool, k, v, layer_bits, semantics="tensor"))
+        if wl.get("outliers"):
+            outliers(k)
+            outliers(v)
+        stores.append(P.pack_dense(pool, k, v, layer_bits, semantics="tensor"))
     del k, v
-    q = torch.randn((wl["layers"], wl["batch"], wl["q_heads"], 1, wl["dim"]), generator=gen,
+    q = torch.randn((wl["layers"], batch, wl["q_heads"], 1, wl["dim"]), generator=gen,
                     device=device, dtype=torch.float32).half()
     torch.cuda.synchronize(device)
+    layers = [stores[l % distinct] for l in range(wl["layers"])]
     kv_bytes = [t.resident_bytes() for t in layers]
     return pool, layers, q, kv_bytes
 
@@ -218,8 +256,13 @@ def run_ours(args, wl):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
-    pool, layers, q, kv_bytes = build_workload(wl, device, seed=1234 + rank)
-    L, B, Hq, D = wl["layers"], wl["batch"], wl["q_heads"], wl["dim"]
+    strong = bool(wl.get("strong"))
+    B = wl["batch"] // world if strong else wl["batch"]  # sequences this rank decodes
+    if strong and wl["batch"] % world:
+        raise SystemExit(f"{wl['batch']} sequences do not split evenly over {world} GPUs")
+    distinct = max(1, min(wl["layers"], int(STORE_BUDGET // layer_store_bytes(wl, B))))
+    pool, layers, q, kv_bytes = build_workload(wl, device, seed=1234 + rank, batch=B, distinct=distinct)
+    L, Hq, D = wl["layers"], wl["q_heads"], wl["dim"]
     splits, scale = wl["splits"], 1 / math.sqrt(D)
     io_bytes = q[0].numel() * 2 * 2  # queries in + outputs out, per layer
     step_bytes = sum(kv_bytes) + L * io_bytes
@@ -317,8 +360,10 @@ def run_ours(args, wl):
         line = {
             "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 operands, f32 accumulation", "data": "synthetic (seeded fp16 N(0,1))",
+            "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
+            "dtype": "f16 operands, f32 accumulation",
+            "data": "synthetic (seeded fp16 N(0,1)" + (", 4 outlier channels per head x(+-8))" if wl.get("outliers")
+                                                        else ")"),
             "config": {
                 "workload": wl["name"], "layers": L, "q_heads": Hq, "kv_heads": wl["kv_heads"],
                 "head_dim": D, "batch_per_gpu": B, "context_tokens": wl["tokens"], "page_tokens": 16,
@@ -326,6 +371,7 @@ def run_ours(args, wl):
                                   "evicted": wl["mix"][0]},
                 "scale_group": wl["group"], "split_k": splits,
                 "kv_pool_gb_per_gpu": round(pool.nbytes / 1e9, 2),
+                "distinct_layer_stores": distinct,
                 "parallelism": f"batch-sharded x{world} (independent sequences, no collective)",
                 "l2": "inputs larger than L2 (KV pool >> 126 MB), no flush needed",
             },
