@@ -8,6 +8,8 @@ Mirrors the reference's model-side integration in
 ``model_gate`` (:294-313), whose acceptance rule is the parity check here: over
 the same stores, the packed route's logits stay within a mean per-token KL of
 0.002 of the dense route's, and the FP16 paged route matches the stock model.
+``controlled_decode`` is the reference's fixed-history timing harness
+(``src/anchorkv/benchmark_suite.py:155-264``).
 
 Model code (``transformers``) is imported lazily: it is needed only when a
 model runs.
@@ -172,3 +174,112 @@ def model_gate(model, source, first_token, forced, settings):
         checks.append({"policy": policy, "mean_kl_dense_vs_packed": discrepancy,
                        "max_logit_error": float((dense - packed).abs().max())})
     return checks
+
+
+CONTROLLED_POLICIES = ("native_fp16", "paged_fp16", "int8", "int4", "automatic", "recent", "random", "oracle")
+
+
+def controlled_decode(model, source, settings, policy, input_tokens, measured_tokens, warmup_tokens=32,
+                      protected=(), backend="packed"):
+    """Fixed-history decode throughput and cache lifecycle
+    (benchmark_suite.controlled_decode, benchmark_suite.py:155-264): the
+    ``warmup_tokens`` then ``measured_tokens`` of ``input_tokens`` are appended
+    one decode step at a time after the ``source`` prefix; no sampling, no
+    logit transfers.  ``measured_cuda_timeline_seconds`` is device-timeline
+    time between two events (launch gaps included).  Returns the reference's
+    row fields."""
+    import gc
+    import hashlib
+    import json
+    import time
+
+    total = warmup_tokens + measured_tokens
+    if warmup_tokens < 0 or measured_tokens <= 0 or len(input_tokens) != total:
+        raise ValueError("provide exactly warmup_tokens + measured_tokens input tokens")
+    if policy not in CONTROLLED_POLICIES:
+        raise ValueError("unknown policy")
+    device = model.device
+    gpu = device.type == "cuda"
+    if not gpu and backend == "packed" and policy != "native_fp16":
+        raise ValueError("packed throughput requires CUDA")
+    native = policy == "native_fp16"
+    bits = 16 if policy == "paged_fp16" else 8 if policy == "int8" else 4
+
+    def synchronize():
+        if gpu:
+            torch.cuda.synchronize(device)
+
+    def report(cache):
+        if not native:
+            return cache.report()
+        size = sum(t.numel() * t.element_size() for layer in cache.layers for t in (layer.keys, layer.values))
+        return {"tokens": cache.get_seq_length(), "resident_bytes": size, "payload_bytes": size, "demotions": 0}
+
+    gc.collect()
+    if gpu:
+        torch.cuda.empty_cache()
+    prefix = source[0][0].shape[-2]
+    ids = torch.tensor([input_tokens], device=device, dtype=torch.long)
+    positions = torch.arange(prefix, prefix + total, device=device)
+    synchronize()
+    base_allocated = torch.cuda.memory_allocated(device) if gpu else None
+    if gpu:
+        torch.cuda.reset_peak_memory_stats(device)
+    started = time.perf_counter()
+    with torch.inference_mode():
+        cache = (stock_cache(source, device=device) if native else
+                 make_live_cache(source, settings, protected, bits, max_tokens=prefix + total, device=device))
+        synchronize()
+        setup_seconds = time.perf_counter() - started
+        initial = report(cache)
+
+        def step(index):
+            output = model(input_ids=ids[:, index:index + 1], past_key_values=cache,
+                           cache_position=positions[index:index + 1], use_cache=True,
+                           attention_mask=None if native else {"full_attention": None}, logits_to_keep=1)
+            del output
+
+        with attention_route(model, None if native else cache, backend):
+            warm_started = time.perf_counter()
+            for index in range(warmup_tokens):
+                step(index)
+            synchronize()
+            warmup_seconds = time.perf_counter() - warm_started
+            before = report(cache)
+            setup_warmup_peak = torch.cuda.max_memory_allocated(device) if gpu else None
+            if gpu:
+                torch.cuda.reset_peak_memory_stats(device)
+                begin = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+            measured_started = time.perf_counter()
+            if gpu:
+                begin.record()
+            for index in range(warmup_tokens, total):
+                step(index)
+            if gpu:
+                end.record()
+            synchronize()
+            wall_seconds = time.perf_counter() - measured_started
+            cuda_seconds = begin.elapsed_time(end) / 1000 if gpu else None
+        final = report(cache)
+        peak = torch.cuda.max_memory_allocated(device) if gpu else None
+        end_allocated = torch.cuda.memory_allocated(device) if gpu else None
+    assert final["tokens"] == prefix + total, "decode did not append the complete fixed workload"
+    row = {"policy": policy, "backend": "stock_sdpa" if native else backend,
+           "scope": "fixed-history throughput and cache lifecycle; not answer accuracy",
+           "prefix_tokens": prefix, "warmup_tokens": warmup_tokens, "measured_tokens": measured_tokens,
+           "setup_seconds": setup_seconds, "warmup_seconds": warmup_seconds,
+           "measured_wall_seconds": wall_seconds, "measured_cuda_timeline_seconds": cuda_seconds,
+           "steady_tokens_per_second": measured_tokens / wall_seconds,
+           "setup_warmup_decode_seconds": setup_seconds + warmup_seconds + wall_seconds,
+           "initial_cache": initial, "measurement_start_cache": before, "final_cache": final,
+           "new_measured_demotions": final["demotions"] - before["demotions"],
+           "setup_warmup_peak_allocated_bytes": setup_warmup_peak, "measured_peak_allocated_bytes": peak,
+           "measured_peak_incremental_bytes": peak - base_allocated if gpu else None,
+           "end_incremental_bytes": end_allocated - base_allocated if gpu else None,
+           "input_sha256": hashlib.sha256(json.dumps(input_tokens).encode()).hexdigest()}
+    del cache, ids, positions
+    gc.collect()
+    if gpu:
+        torch.cuda.empty_cache()
+    return row

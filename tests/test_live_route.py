@@ -75,3 +75,44 @@ def test_live_cache_appends_and_demotes_during_decode(cuda):
     assert after["tokens"] == before["tokens"] + 40 == 139
     assert after["demotions"] > before["demotions"]
     assert after["payload_bytes"] < 2 * 2 * 2 * 8 * 139 * 128  # below the FP16 size of two layers' K and V
+
+
+def test_controlled_decode_validates_like_the_reference():
+    model = _qwen3(32, 4, 2, 1, "cpu", torch.float32)
+    source = [(torch.zeros(1, 2, 16, 32), torch.zeros(1, 2, 16, 32))]
+    with pytest.raises(ValueError, match="provide exactly"):
+        live.controlled_decode(model, source, live.Settings(), "int4", [1, 2, 3], 2, warmup_tokens=2)
+    with pytest.raises(ValueError, match="unknown policy"):
+        live.controlled_decode(model, source, live.Settings(), "int2", [1, 2, 3], 1, warmup_tokens=2)
+    with pytest.raises(ValueError, match="packed throughput requires CUDA"):
+        live.controlled_decode(model, source, live.Settings(), "int4", [1, 2, 3], 1, warmup_tokens=2)
+
+
+@torch.inference_mode()
+def test_controlled_decode_native_on_cpu():
+    model = _qwen3(32, 4, 2, 2, "cpu", torch.float32)
+    ids = torch.randint(0, 2048, (1, 20), generator=torch.Generator().manual_seed(5))
+    source = live.cache_cpu(model(input_ids=ids, use_cache=True, logits_to_keep=1).past_key_values)
+    row = live.controlled_decode(model, source, live.Settings(), "native_fp16", list(range(6)), 4,
+                                 warmup_tokens=2)
+    assert row["final_cache"]["tokens"] == 26 and row["measured_cuda_timeline_seconds"] is None
+    assert row["backend"] == "stock_sdpa" and row["new_measured_demotions"] == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prefix", [128, 256, 512])
+def test_controlled_decode_packed_cache_lifecycle(cuda, prefix):
+    """The fixed-history workloads at 128/256/512-token prefixes: every measured
+    token is appended, archived pages are demoted on the way, and the INT4 store
+    stays below the stock FP16 cache."""
+    model = _qwen3(128, 16, 8, 2, cuda, torch.float16)
+    ids = torch.randint(0, 2048, (1, prefix), generator=torch.Generator().manual_seed(6))
+    with torch.inference_mode():
+        source = live.cache_cpu(model(input_ids=ids.to(cuda), use_cache=True, logits_to_keep=1).past_key_values)
+    tokens = torch.randint(0, 2048, (48,), generator=torch.Generator().manual_seed(7)).tolist()
+    packed = live.controlled_decode(model, source, live.Settings(), "int4", tokens, 32, warmup_tokens=16)
+    native = live.controlled_decode(model, source, live.Settings(), "native_fp16", tokens, 32, warmup_tokens=16)
+    assert packed["final_cache"]["tokens"] == native["final_cache"]["tokens"] == prefix + 48
+    assert packed["new_measured_demotions"] > 0
+    assert packed["final_cache"]["payload_bytes"] < native["final_cache"]["payload_bytes"]
+    assert packed["measured_cuda_timeline_seconds"] > 0 and packed["steady_tokens_per_second"] > 0
