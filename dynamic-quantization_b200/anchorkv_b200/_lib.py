@@ -42,6 +42,13 @@ PROTOTYPES = {
     "akv_decode_partials": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, _c_p, _i32, _c_p, _i64, _i64,
                                            _i32, _i32, _i32, _i32, _i32, _f32, _i32, _c_p, _i64, _c_p,
                                            _c_p]),
+    "akv_exchange_bytes": (_i64, [_i32, _i32, _i32, _i32]),
+    "akv_merge_exchange": (ctypes.c_int, [_c_p, _i32, _i32, _i32, _c_p, _i32, _i32, ctypes.c_uint32, _c_p, _i64,
+                                          _i64, _c_p, _c_p]),
+    "akv_ipc_alloc": (ctypes.c_int, [_i64, ctypes.POINTER(_c_p), _c_p]),
+    "akv_ipc_open": (ctypes.c_int, [_c_p, ctypes.POINTER(_c_p)]),
+    "akv_ipc_close": (ctypes.c_int, [_c_p]),
+    "akv_ipc_free": (ctypes.c_int, [_c_p]),
     "akv_merge": (ctypes.c_int, [_c_p, _i32, _i32, _i32, _c_p, _i64, _i64, _c_p, _c_p, _c_p]),
     "akv_merge_states": (ctypes.c_int, [_c_p, _i32, _i32, _i32, _i32, _c_p, _i64, _i64, _c_p]),
     "akv_packed_attention": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, _c_p, _i32, _c_p, _i64, _i64,

@@ -14,14 +14,22 @@ and merges their (max, sum-exp, accumulator) states by log-sum-exp
 No KV page ever crosses GPUs; the collective moves only the small states.
 Batched decode needs none of this: sequences are independent, so a batch is
 split across ranks with no collective at all.
+
+:class:`PeerExchange` does the same exchange without a library collective:
+one kernel per call (``akv_merge_exchange``) merges this rank's partials, stores
+the state into every rank's buffer over NVLink, waits (bounded) for the other
+ranks' states and merges them (buffers shared through CUDA IPC).
 """
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
-from .decode import decode_partial_states, merge_states
+from . import _lib
+from .decode import _store_geometry, _workspace, decode_partial_states, merge_states
 
 
 def shard_range(n_blocks: int, rank: int, world: int) -> tuple[int, int]:
@@ -54,3 +62,85 @@ def sharded_packed_attention(query, local_store, scale, *, splits=0, group=None,
     the collective logic can be exercised with host stand-ins."""
     state = local_states(query, local_store, scale, splits=splits)
     return merge(gather_states(state, group))
+
+
+class PeerExchange:
+    """Cross-GPU LSE merge over peer memory for sequences split over the ranks
+    of ``group`` (one process per GPU of one node, at most 8).
+
+    Every rank allocates an exchange buffer (``akv_exchange_bytes``), the
+    ranks trade CUDA IPC handles through the process group, and each rank
+    maps the others' buffers.  :meth:`attention` then decodes this rank's
+    pages and runs ``akv_merge_exchange``: the output of the whole sequence,
+    on every rank, in two kernel launches and no library collective.  Every
+    rank must make the same calls; :meth:`close` (collective) unmaps and frees.
+    """
+
+    def __init__(self, batch: int, q_heads: int, dim: int, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.batch, self.q_heads, self.dim = batch, q_heads, dim
+        lib = _lib.load()
+        nbytes = lib.akv_exchange_bytes(self.world, batch, q_heads, dim)
+        if nbytes < 0:
+            raise ValueError("unsupported exchange geometry (at most 8 ranks, head_dim 64 or 128)")
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        _lib.call("akv_ipc_alloc", nbytes, ctypes.byref(own), handle)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._own = own.value
+        self._mapped = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self._own)
+                continue
+            peer = ctypes.c_void_p()
+            _lib.call("akv_ipc_open", ctypes.create_string_buffer(h, 64), ctypes.byref(peer))
+            self._mapped.append(peer.value)
+            ptrs.append(peer.value)
+        self._peers = (ctypes.c_void_p * self.world)(*ptrs)
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def attention(self, query, local_store, scale, *, splits=0, out=None):
+        """Decode this rank's pages of each sequence and merge with the other
+        ranks: the full-context output ``[batch, Hq, 1, D]`` on every rank."""
+        if tuple(query.shape) != (self.batch, self.q_heads, 1, self.dim):
+            raise ValueError("query shape differs from the exchange's geometry")
+        query = query.contiguous()
+        arena, arena_bytes, table, seq_blocks, max_blocks = _store_geometry(local_store)
+        dev = query.device
+        lib = _lib.load()
+        nbytes = lib.akv_workspace_bytes(self.batch, self.q_heads, local_store.heads, self.dim, max_blocks,
+                                         splits)
+        if nbytes < 0:
+            raise ValueError("unsupported decode geometry")
+        ws = _workspace(dev, nbytes)
+        if out is None:
+            out = torch.empty_like(query)
+        stream = _lib.stream_of(dev)
+        status = _lib.status_word(dev).data_ptr()
+        _lib.call("akv_decode_partials", arena.data_ptr(), arena_bytes, table.data_ptr(), table.stride(0),
+                  None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks, query.data_ptr(),
+                  query.stride(0), query.stride(1), self.batch, self.q_heads, local_store.heads, self.dim,
+                  local_store.group, float(scale), splits, ws.data_ptr(), ws.numel(), status, stream)
+        self.epoch += 1
+        _lib.call("akv_merge_exchange", ws.data_ptr(), self.batch, self.q_heads, self.dim, self._peers,
+                  self.rank, self.world, self.epoch, out.data_ptr(), out.stride(0), out.stride(1), status,
+                  stream)
+        return out
+
+    def close(self):
+        """Collective: wait for every rank's kernels, then unmap and free."""
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for ptr in self._mapped:
+            _lib.call("akv_ipc_close", ctypes.c_void_p(ptr))
+        self._mapped = []
+        dist.barrier(group=self.group)
+        if self._own:
+            _lib.call("akv_ipc_free", ctypes.c_void_p(self._own))
+            self._own = None

@@ -39,6 +39,8 @@
 //    decomposition, so merging needs nothing but the workspace.
 #include <math.h>
 
+#include <string.h>
+
 #include <algorithm>
 #include <mutex>
 
@@ -820,6 +822,42 @@ __global__ void __launch_bounds__(128) merge_rows_kernel(const int32_t *__restri
   store_row<D>(lane, b, h, q_heads, m, l, acc, out, obs, ohs, state);
 }
 
+// Fold contributors w, w + stride, ... (<= w_end) of `item`, query head n of its
+// group, into (m, l, acc): every load of a contributor is issued before its
+// weight is tested (two in flight per loop trip), and each contributor's first
+// item advances incrementally.
+template <int D>
+__device__ __forceinline__ void fold_partials(const MergeGeom &g, int item, int n, int w, int w_end, int stride,
+                                              int lane, float &m, float &l, float (&acc)[D / 32]) {
+  constexpr int PS = D + 4, VEC = D / 32;
+  if (w > w_end) return;
+  int first = w * g.range / g.mb, rem = w * g.range - first * g.mb;
+  const int step = stride * g.range, sq = step / g.mb, sr = step - sq * g.mb;
+#pragma unroll 2
+  for (; w <= w_end; w += stride) {
+    const float *pr = g.partials + ((int64_t)(w * g.smax + (item - first)) * g.slot_heads + n) * PS;
+    const float mw = __ldcg(pr + D), lw = __ldcg(pr + D + 1);
+    float a[VEC];
+    if constexpr (VEC == 4) {
+      const float4 v = __ldcg(reinterpret_cast<const float4 *>(pr) + lane);
+      a[0] = v.x, a[1] = v.y, a[2] = v.z, a[3] = v.w;
+    } else {
+      const float2 v = __ldcg(reinterpret_cast<const float2 *>(pr) + lane);
+      a[0] = v.x, a[1] = v.y;
+    }
+    if (mw != -INFINITY) {  // an empty share weighs 0 (triton_decode.py:78)
+      const float top = fmaxf(m, mw);
+      const float c = ex2(m - top), e = ex2(mw - top);
+      l = l * c + e * lw;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * c + e * a[i];
+      m = top;
+    }
+    first += sq, rem += sr;
+    if (rem >= g.mb) rem -= g.mb, ++first;
+  }
+}
+
 // The same merge for rows with hundreds of contributors (a long single
 // sequence): one CTA of 32 warps per row, warp w folds contributors w, w+32, ...
 // and the warps combine in shared memory.
@@ -846,36 +884,8 @@ __global__ void __launch_bounds__(1024) merge_wide_kernel(const int32_t *__restr
   for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
   if (g.mb > 0) {
     const int w0 = item * g.mb / g.range;
-    const int w1 = min(((item + 1) * g.mb - 1) / g.range, g.warps - 1);
-    int w = w0 + warp;
-    if (w <= w1) {
-      // first item of contributor w, advanced incrementally by W contributors
-      int first = w * g.range / g.mb, rem = w * g.range - first * g.mb;
-      const int stride = W * g.range, sq = stride / g.mb, sr = stride - sq * g.mb;
-#pragma unroll 2
-      for (; w <= w1; w += W) {
-        const float *pr = g.partials + ((int64_t)(w * g.smax + (item - first)) * g.slot_heads + n) * PS;
-        const float mw = __ldcg(pr + D), lw = __ldcg(pr + D + 1);
-        float a[VEC];
-        if constexpr (VEC == 4) {
-          const float4 v = __ldcg(reinterpret_cast<const float4 *>(pr) + lane);
-          a[0] = v.x, a[1] = v.y, a[2] = v.z, a[3] = v.w;
-        } else {
-          const float2 v = __ldcg(reinterpret_cast<const float2 *>(pr) + lane);
-          a[0] = v.x, a[1] = v.y;
-        }
-        if (mw != -INFINITY) {  // an empty share weighs 0 (triton_decode.py:78)
-          const float top = fmaxf(m, mw);
-          const float c = ex2(m - top), e = ex2(mw - top);
-          l = l * c + e * lw;
-#pragma unroll
-          for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * c + e * a[i];
-          m = top;
-        }
-        first += sq, rem += sr;
-        if (rem >= g.mb) rem -= g.mb, ++first;
-      }
-    }
+    fold_partials<D>(g, item, n, w0 + warp, min(((item + 1) * g.mb - 1) / g.range, g.warps - 1), W, lane, m, l,
+                     acc);
   }
 #pragma unroll
   for (int i = 0; i < VEC; ++i) sm_acc[warp][VEC * lane + i] = acc[i];
@@ -897,6 +907,128 @@ __global__ void __launch_bounds__(1024) merge_wide_kernel(const int32_t *__restr
     }
     store_row<D>(lane, b, h, q_heads, top, den, num, out, obs, ohs, state);
   }
+}
+
+// ======================================== cross-GPU merge over peer memory
+// One long sequence split over `world` GPUs: every rank decodes its page range
+// into partial states, then this kernel, per (sequence, query head) row,
+// (1) merges the rank's partials into one state (as merge_wide_kernel),
+// (2) stores that state into every rank's exchange buffer over NVLink (plain
+//     peer stores) and raises the row's flag there with a system-scope release,
+// (3) waits (bounded) until every rank's flag for the row carries this call's
+//     epoch, and (4) merges the world's states into the output.
+// A row's wait depends only on the same row's CTA on the other GPUs, which
+// stores before it waits, so no CTA waits on one that cannot run.
+//
+// Exchange buffer of one rank (akv_exchange_bytes): fp32 states
+// [world][rows][D+2] (slot r holds rank r's state of every row), then uint32
+// flags [world][rows] (flag [r][row] = the epoch of the last call whose rank-r
+// state of the row has landed).  Buffers start zeroed; epochs start at 1.
+constexpr int kMaxPeers = 8;
+struct PeerBuffers {
+  void *buf[kMaxPeers];
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int D>
+__global__ void __launch_bounds__(1024) merge_exchange_kernel(const int32_t *__restrict__ header, int q_heads,
+                                                              PeerBuffers peers, int rank, int world,
+                                                              uint32_t epoch, __half *__restrict__ out,
+                                                              int64_t obs, int64_t ohs, int32_t *status) {
+  constexpr int PS = D + 4, VEC = D / 32, W = 32, RS = D + 2;
+  __shared__ float sm_acc[W][D];
+  __shared__ float sm_m[W], sm_l[W];
+  grid_dependency_wait();
+  MergeGeom g;
+  if (!merge_geom<D>(header, g)) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+    return;
+  }
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = h / g.gqa, r = h - kvh * g.gqa, qg = r >> 3, n = r & 7;
+  const int item = (b * g.kv_heads + kvh) * g.qgroups + qg;
+  float m = -INFINITY, l = 0.f, acc[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
+  if (g.mb > 0) {  // (1) this rank's partials, warp w folding contributors w, w + 32, ...
+    const int w0 = item * g.mb / g.range;
+    fold_partials<D>(g, item, n, w0 + warp, min(((item + 1) * g.mb - 1) / g.range, g.warps - 1), W, lane, m, l,
+                     acc);
+  }
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) sm_acc[warp][VEC * lane + i] = acc[i];
+  if (lane == 0) sm_m[warp] = m, sm_l[warp] = l;
+  __syncthreads();
+  if (warp != 0) return;
+  float top = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < W; ++k) top = fmaxf(top, sm_m[k]);
+  float num[VEC], den = 0.f;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) num[i] = 0.f;
+#pragma unroll 8
+  for (int k = 0; k < W; ++k) {
+    const float e = sm_m[k] == -INFINITY ? 0.f : ex2(sm_m[k] - top);
+    den += e * sm_l[k];
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) num[i] += e * sm_acc[k][VEC * lane + i];
+  }
+  const int rows = gridDim.x * gridDim.y, row = b * q_heads + h;
+  const int64_t flag_offset = (int64_t)world * rows * RS;  // in floats
+  // (2) publish to every rank, this one included
+  for (int pr = 0; pr < world; ++pr) {
+    float *st = reinterpret_cast<float *>(peers.buf[pr]) + ((int64_t)rank * rows + row) * RS;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) st[VEC * lane + i] = num[i];
+    if (lane == 0) st[D] = top, st[D + 1] = den;
+  }
+  __threadfence_system();  // each lane's state stores before any flag
+  __syncwarp();
+  if (lane < world)
+    st_release_sys(reinterpret_cast<uint32_t *>(reinterpret_cast<float *>(peers.buf[lane]) + flag_offset) +
+                       (int64_t)rank * rows + row,
+                   epoch);
+  // (3) bounded wait for every rank's state of this row (lane q watches rank q)
+  const float *mine = reinterpret_cast<const float *>(peers.buf[rank]);
+  const uint32_t *flags = reinterpret_cast<const uint32_t *>(mine + flag_offset);
+  bool ok = true;
+  if (lane < world) {
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_sys(flags + (int64_t)lane * rows + row) != epoch)
+      if (globaltimer() - t0 > kWaitNs) {
+        ok = false;
+        break;
+      }
+  }
+  if (!__all_sync(0xffffffffu, ok)) {
+    if (lane == 0) set_status(status, AKV_DEV_TIMEOUT);
+    return;
+  }
+  // (4) merge the world's states (each lane re-acquires the flag it reads behind)
+  float mt = -INFINITY, lt = 0.f, at[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) at[i] = 0.f;
+  for (int q = 0; q < world; ++q) {
+    (void)ld_acquire_sys(flags + (int64_t)q * rows + row);
+    const float *st = mine + ((int64_t)q * rows + row) * RS;
+    const float mq = __ldcg(st + D), lq = __ldcg(st + D + 1);
+    if (mq == -INFINITY) continue;
+    const float tp = fmaxf(mt, mq), c = ex2(mt - tp), e = ex2(mq - tp);
+    lt = lt * c + e * lq;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) at[i] = at[i] * c + e * __ldcg(st + VEC * lane + i);
+    mt = tp;
+  }
+  store_row<D>(lane, b, h, q_heads, mt, lt, at, out, obs, ohs, nullptr);
 }
 
 // Merge n already-merged states laid out [n][batch][q_heads][D+2] (e.g. gathered
@@ -1112,6 +1244,66 @@ extern "C" int akv_merge(const void *workspace, int32_t batch, int32_t q_heads, 
                                          out_head_stride, state_out, dev_status, s);
   return err == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
 }
+
+extern "C" int64_t akv_exchange_bytes(int32_t world, int32_t batch, int32_t q_heads, int32_t head_dim) {
+  if (world <= 0 || world > kMaxPeers || batch <= 0 || q_heads <= 0 || (head_dim != 64 && head_dim != 128))
+    return -1;
+  const int64_t rows = (int64_t)batch * q_heads;
+  return world * rows * (head_dim + 2) * 4 + world * rows * 4;
+}
+
+extern "C" int akv_merge_exchange(const void *workspace, int32_t batch, int32_t q_heads, int32_t head_dim,
+                                  void *const *peer_buffers, int32_t rank, int32_t world, uint32_t epoch,
+                                  void *out, int64_t out_batch_stride, int64_t out_head_stride,
+                                  int32_t *dev_status, void *stream) {
+  if (!workspace || !peer_buffers || !out || epoch == 0) return AKV_ERR_INVALID;
+  if (akv_exchange_bytes(world, batch, q_heads, head_dim) < 0 || rank < 0 || rank >= world || batch > 65535)
+    return head_dim != 64 && head_dim != 128 ? AKV_ERR_UNSUPPORTED : AKV_ERR_INVALID;
+  PeerBuffers peers = {};
+  for (int r = 0; r < world; ++r) {
+    if (!peer_buffers[r] || ((uintptr_t)peer_buffers[r] & 15)) return AKV_ERR_INVALID;
+    peers.buf[r] = peer_buffers[r];
+  }
+  const int32_t *header = (const int32_t *)workspace;
+  cudaStream_t s = (cudaStream_t)stream;
+  const dim3 grid(q_heads, batch);
+  const cudaError_t err =
+      head_dim == 64 ? launch_dependent(merge_exchange_kernel<64>, grid, 1024, 0, s, header, (int)q_heads, peers,
+                                        (int)rank, (int)world, epoch, (__half *)out, out_batch_stride,
+                                        out_head_stride, dev_status)
+                     : launch_dependent(merge_exchange_kernel<128>, grid, 1024, 0, s, header, (int)q_heads, peers,
+                                        (int)rank, (int)world, epoch, (__half *)out, out_batch_stride,
+                                        out_head_stride, dev_status);
+  return err == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+}
+
+extern "C" int akv_ipc_alloc(int64_t bytes, void **ptr, void *handle) {
+  if (bytes <= 0 || !ptr || !handle) return AKV_ERR_INVALID;
+  void *p = nullptr;
+  if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) return AKV_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, (size_t)bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return AKV_ERR_CUDA;
+  }
+  static_assert(sizeof(h) == AKV_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return AKV_OK;
+}
+
+extern "C" int akv_ipc_open(const void *handle, void **ptr) {
+  if (!handle || !ptr) return AKV_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+}
+
+extern "C" int akv_ipc_close(void *ptr) {
+  return ptr && cudaIpcCloseMemHandle(ptr) == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+}
+
+extern "C" int akv_ipc_free(void *ptr) { return ptr && cudaFree(ptr) == cudaSuccess ? AKV_OK : AKV_ERR_CUDA; }
 
 extern "C" int akv_merge_states(const float *states, int32_t n, int32_t batch, int32_t q_heads,
                                 int32_t head_dim, void *out, int64_t out_batch_stride,

@@ -157,6 +157,38 @@ int akv_merge_states(const float *states, int32_t n, int32_t batch, int32_t q_he
                      int32_t head_dim, void *out, int64_t out_batch_stride,
                      int64_t out_head_stride, void *stream);
 
+/* Bytes of one rank's exchange buffer for akv_merge_exchange (-1 if invalid):
+ * fp32 states [world][batch * q_heads][head_dim + 2] then uint32 flags
+ * [world][batch * q_heads].  world <= 8. */
+int64_t akv_exchange_bytes(int32_t world, int32_t batch, int32_t q_heads, int32_t head_dim);
+
+/* Cross-GPU merge over peer memory for one sequence split over `world` GPUs
+ * (each rank decoded its page range into `workspace` with akv_decode_partials):
+ * one kernel merges this rank's partials per (sequence, query head), stores the
+ * state into every rank's exchange buffer (plain peer stores over NVLink),
+ * raises the row's flag there, waits (bounded, AKV_DEV_TIMEOUT after 2 s) for
+ * every rank's flag of the row, and merges the world's states into `out`.
+ * Replaces akv_merge + an all-gather + akv_merge_states.
+ *   peer_buffers[r]: rank r's exchange buffer as mapped in this process
+ *     (akv_ipc_alloc / akv_ipc_open), zeroed before the first call;
+ *   epoch: 1 for the first call on these buffers, +1 for each following call,
+ *     the same on every rank.  Every rank must make the same calls. */
+int akv_merge_exchange(const void *workspace, int32_t batch, int32_t q_heads, int32_t head_dim,
+                       void *const *peer_buffers, int32_t rank, int32_t world, uint32_t epoch, void *out,
+                       int64_t out_batch_stride, int64_t out_head_stride, int32_t *dev_status,
+                       void *stream);
+
+/* Device buffers shared between the processes of one node (CUDA IPC).  No
+ * counterpart in the reference.  akv_ipc_alloc allocates `bytes` zeroed bytes
+ * on the current device and writes its AKV_IPC_HANDLE_BYTES-byte handle;
+ * another process maps it with akv_ipc_open and unmaps it with akv_ipc_close;
+ * the owner frees it with akv_ipc_free after every mapping is closed. */
+#define AKV_IPC_HANDLE_BYTES 64
+int akv_ipc_alloc(int64_t bytes, void **ptr, void *handle);
+int akv_ipc_open(const void *handle, void **ptr);
+int akv_ipc_close(void *ptr);
+int akv_ipc_free(void *ptr);
+
 /* akv_decode_partials followed by akv_merge, partials in the caller's workspace
  * (at least akv_workspace_bytes bytes, 16-byte aligned).  Both kernels are
  * launched as programmatic dependents of their predecessor in the stream, so

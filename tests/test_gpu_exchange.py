@@ -1,0 +1,150 @@
+"""Cross-GPU LSE merge over peer memory (akv_merge_exchange, PeerExchange):
+the long-context exchange of the reference's split-K merge
+(triton_decode.py:70-82) across GPUs, against the oracle.
+
+Single-GPU cases call the kernel with one rank, or make its bounded wait run
+out on a flag nothing sets; the two-rank case runs as two child processes, one
+GPU each (skipped with fewer GPUs), with NVLS off."""
+
+import ctypes
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import anchorkv_b200 as akv
+import workloads as W
+from anchorkv_b200 import _lib
+from anchorkv_b200 import pool as P
+from paged_reference import paged_decode_f64
+
+pytestmark = pytest.mark.gpu
+
+HQ, HKV, D, PAGES = 32, 8, 128, 300
+
+
+def _sequence(seed=41):
+    k = W.outlier_kv(seed, (1, HKV, 16 * PAGES, D))
+    v = W.outlier_kv(seed + 1, (1, HKV, 16 * PAGES, D))
+    q = W.normal(seed + 2, (1, HQ, 1, D))
+    bits = np.array(W.draw_modes(seed + 3, PAGES, {16: .05, 8: .25, 4: .7}))[None]
+    return k, v, q, bits
+
+
+def _store(device, k, v, bits, lo, hi):
+    sub = bits[:, lo:hi]
+    pool = P.PagePool(HKV, D, group=2048, pages={b: int((sub == b).sum()) for b in (16, 8, 4)}, device=device)
+    return P.pack_dense(pool, k[:, :, 16 * lo:16 * hi].to(device), v[:, :, 16 * lo:16 * hi].to(device), sub)
+
+
+def _buffer(world):
+    lib = _lib.load()
+    ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+    _lib.call("akv_ipc_alloc", lib.akv_exchange_bytes(world, 1, HQ, D), ctypes.byref(ptr), handle)
+    return ptr.value
+
+
+def _decode(store, q, ws):
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    _lib.call("akv_decode_partials", store.pool.arena.data_ptr(), store.pool.nbytes, store.table.data_ptr(),
+              store.table.stride(0), store.seq_blocks.data_ptr(), store.max_blocks, q.data_ptr(), q.stride(0),
+              q.stride(1), 1, HQ, HKV, D, 2048, 0.088, 0, ws.data_ptr(), ws.numel(),
+              _lib.status_word(q.device).data_ptr(), stream)
+
+
+def test_single_rank_exchange_equals_packed_attention(cuda):
+    k, v, q, bits = _sequence()
+    store = _store(cuda, k, v, bits, 0, PAGES)
+    qd = q.to(cuda)
+    ref = akv.packed_attention(qd, store, 0.088, splits=0)
+    lib = _lib.load()
+    ws = torch.empty(lib.akv_workspace_bytes(1, HQ, HKV, D, PAGES, 0), dtype=torch.uint8, device=cuda)
+    own = _buffer(1)
+    peers = (ctypes.c_void_p * 1)(own)
+    for epoch in (1, 2, 3):
+        out = torch.full_like(qd, float("nan"))
+        _decode(store, qd, ws)
+        _lib.call("akv_merge_exchange", ws.data_ptr(), 1, HQ, D, peers, 0, 1, epoch, out.data_ptr(), out.stride(0),
+                  out.stride(1), _lib.status_word(cuda).data_ptr(), torch.cuda.current_stream(cuda).cuda_stream)
+        torch.testing.assert_close(out, ref, atol=1e-3, rtol=1e-3)
+    assert akv.take_device_status(cuda) == 0
+    _lib.call("akv_ipc_free", ctypes.c_void_p(own))
+
+
+def test_exchange_wait_runs_out_and_reports(cuda):
+    """Rank 0 of a two-rank exchange whose other rank never publishes: the
+    flag nothing sets makes the bounded wait give up (2 s), the status word
+    reports AKV_DEV_TIMEOUT and the context stays usable."""
+    k, v, q, bits = _sequence()
+    store = _store(cuda, k, v, bits, 0, PAGES // 2)
+    qd = q.to(cuda)
+    lib = _lib.load()
+    ws = torch.empty(lib.akv_workspace_bytes(1, HQ, HKV, D, store.max_blocks, 0), dtype=torch.uint8, device=cuda)
+    own, silent = _buffer(2), _buffer(2)
+    peers = (ctypes.c_void_p * 2)(own, silent)
+    out = torch.zeros_like(qd)
+    _decode(store, qd, ws)
+    _lib.call("akv_merge_exchange", ws.data_ptr(), 1, HQ, D, peers, 0, 2, 1, out.data_ptr(), out.stride(0),
+              out.stride(1), _lib.status_word(cuda).data_ptr(), torch.cuda.current_stream(cuda).cuda_stream)
+    assert akv.take_device_status(cuda) & 2  # AKV_DEV_TIMEOUT
+    assert (out == 0).all()  # nothing merged
+    assert float(torch.ones(4, device=cuda).sum()) == 4.0  # the context still works
+    for ptr in (own, silent):
+        _lib.call("akv_ipc_free", ctypes.c_void_p(ptr))
+
+
+def _rank_main(rank, world, port, queue):
+    try:
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        import datetime
+
+        import torch.distributed as dist
+
+        from anchorkv_b200.sharded import PeerExchange, shard_range
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=dev)
+        k, v, q, bits = _sequence()
+        lo, hi = shard_range(PAGES, rank, world)
+        store = _store(dev, k, v, bits, lo, hi)
+        ex = PeerExchange(1, HQ, D)
+        outs = [ex.attention(q.to(dev), store, 0.088).float().cpu() for _ in range(3)]
+        status = akv.take_device_status(dev)
+        ex.close()
+        dist.destroy_process_group()
+        queue.put((rank, status, [o.numpy() for o in outs]))
+    except Exception as exc:  # reported to the parent, which fails the test
+        queue.put((rank, -1, repr(exc)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_exchange_against_oracle():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in procs:
+        rank, status, outs = queue.get(timeout=240)
+        results[rank] = (status, outs)
+    for p in procs:
+        p.join(timeout=60)
+    assert all(results[r][0] == 0 for r in results), results
+    k, v, q, bits = _sequence()
+    oracle = paged_decode_f64(q[:, :, 0].numpy(), k.numpy(), v.numpy(), bits, 0.088, group=2048)
+    for r in (0, 1):
+        for out in results[r][1]:
+            np.testing.assert_allclose(out.reshape(-1), oracle.reshape(-1), atol=2e-3, rtol=1e-2)
+    np.testing.assert_array_equal(results[0][1][0], results[1][1][0])
