@@ -521,31 +521,52 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
       raw = __ldg(p.table + (int64_t)bb * p.table_stride + (e - it * mb));
     }
   };
-  int64_t w_src = 0;
-  uint32_t w_rb = 0, w_meta = 0, w_mask = 0;
-  uint32_t w_m4 = 0, w_m8 = 0, w_bnd = 0;  // lanes holding INT4 / INT8 pages; lanes starting an item
+  // Per lane (one page of the window each): the record's source offset, the
+  // bytes of the slot this lane leads (its record, or its record and its
+  // partner's), the partner's source and the slot meta.  w_mask marks the
+  // lanes that lead a slot; a follower travels with its leader.
+  int64_t w_src = 0, w_src2 = 0;
+  uint32_t w_need = 0, w_meta = 0, w_mask = 0;
   auto prepare = [&](int w0, int64_t raw, int nb) {
     const int e = w0 + lane;
     bool ok = false, first = false;
     int mode = AKV_MODE_SKIP;
+    uint32_t rb = 0;
     if (e < e_end) {
       const int it = e / mb, j = e - it * mb;
       first = j == 0;
       mode = j < nb ? desc_mode(raw) : AKV_MODE_SKIP;
-      w_rb = mode == AKV_MODE_FP16 ? rb16 : (mode == AKV_MODE_INT8 ? rb8 : rb4);
+      rb = mode == AKV_MODE_FP16 ? rb16 : (mode == AKV_MODE_INT8 ? rb8 : rb4);
       const int64_t poff = desc_offset(raw);
       ok = mode != AKV_MODE_SKIP;
-      if (ok && ((poff & 15) || poff + (int64_t)p.kv_heads * w_rb > p.arena_bytes)) {
+      if (ok && ((poff & 15) || poff + (int64_t)p.kv_heads * rb > p.arena_bytes)) {
         set_status(p.status, AKV_DEV_BAD_DESCRIPTOR);
         ok = false;
       }
-      w_src = poff + (int64_t)((it % ipb) / p.qgroups) * w_rb;
+      w_src = poff + (int64_t)((it % ipb) / p.qgroups) * rb;
       w_meta = (uint32_t)mode | ((uint32_t)desc_ntok(raw) << 4) | ((uint32_t)(it - first_item) << 16);
     }
-    w_mask = __ballot_sync(0xffffffffu, ok);
-    w_m4 = __ballot_sync(0xffffffffu, ok && mode == AKV_MODE_INT4);
-    w_m8 = __ballot_sync(0xffffffffu, ok && mode == AKV_MODE_INT8);
-    w_bnd = __ballot_sync(0xffffffffu, first);
+    // An INT8 or INT4 page pairs with the next page of its item and mode in
+    // the window: in each (item, mode) group of lanes the 1st and 2nd pages
+    // share a slot, the 3rd and 4th, ...; FP16 pages and an odd page out go
+    // alone.  Item boundaries are the lanes whose page starts an item.
+    const uint32_t m4 = __ballot_sync(0xffffffffu, ok && mode == AKV_MODE_INT4);
+    const uint32_t m8 = __ballot_sync(0xffffffffu, ok && mode == AKV_MODE_INT8);
+    const uint32_t bnd = __ballot_sync(0xffffffffu, first);
+    const uint32_t self = 1u << lane, below = self - 1u, above = ~(below | self);
+    const uint32_t lo_bnd = bnd & (below | self), hi_bnd = bnd & above;
+    const uint32_t item = (lo_bnd ? 0xffffffffu << (31 - __clz(lo_bnd)) : 0xffffffffu) &
+                          (hi_bnd ? (hi_bnd & (0u - hi_bnd)) - 1u : 0xffffffffu);
+    const uint32_t group = (mode == AKV_MODE_INT4 ? m4 : (mode == AKV_MODE_INT8 ? m8 : 0u)) & item;
+    const bool grouped = ok && (group & self);
+    const bool follower = grouped && (__popc(group & below) & 1);
+    const uint32_t next = group & above;
+    const int partner = grouped && !follower && next ? __ffs(next) - 1 : lane;
+    w_src2 = __shfl_sync(0xffffffffu, w_src, partner);
+    const uint32_t pmeta = __shfl_sync(0xffffffffu, w_meta, partner);
+    w_need = partner != lane ? 2u * rb : rb;
+    if (partner != lane) w_meta |= 4u | (((pmeta >> 4) & 31u) << 9);
+    w_mask = __ballot_sync(0xffffffffu, ok && !follower);
   };
   int win0 = e_begin;
   int64_t nxt_raw;
@@ -559,7 +580,7 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
   }
 
   uint32_t head = 0, tail = 0, head_p = 0;  // ring counters (virtual) and write position
-  int issued = 0, consumed = 0;
+  uint32_t issued = 0, consumed = 0;         // slots issued / consumed
   bool timed_out = false;
 
   uint32_t qf[T::kTiles][2];
@@ -626,17 +647,8 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
         prepare(win0, raw, nb);
         continue;
       }
-      const int k = __ffs(w_mask) - 1;
-      // An INT8 or INT4 page takes the next page of its item and mode in the
-      // window as its partner: one slot, one barrier and one softmax step for
-      // both.  FP16 pages go alone (two would not fit the ring).
-      const uint32_t kbit = 1u << k, higher = ~((kbit << 1) - 1u);
-      const uint32_t same = (w_m4 & kbit) ? w_m4 : ((w_m8 & kbit) ? w_m8 : 0u);
-      const uint32_t bnd = w_bnd & higher;  // first lane of the next item, if in the window
-      const uint32_t cand = same & w_mask & higher & (bnd ? (bnd & (0u - bnd)) - 1u : 0xffffffffu);
-      const int k2 = cand ? __ffs(cand) - 1 : k;
-      const uint32_t rb = __shfl_sync(0xffffffffu, w_rb, k);
-      const uint32_t need = cand ? 2u * rb : rb;
+      const int k = __ffs(w_mask) - 1;  // the next slot's leading lane
+      const uint32_t need = __shfl_sync(0xffffffffu, w_need, k);
       // Ring space: virtual byte counters (head, tail) grow monotonically (a
       // warp moves far less than 4 GB per launch) and measure occupancy; the
       // physical write position head_p is tracked beside them (no modulo).
@@ -651,31 +663,32 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
       }
       if (start + need - tail > (uint32_t)T::kRing) break;  // wait for room
       const int64_t src = __shfl_sync(0xffffffffu, w_src, k);
-      const int64_t src2 = __shfl_sync(0xffffffffu, w_src, k2);
+      const int64_t src2 = __shfl_sync(0xffffffffu, w_src2, k);
       const uint32_t meta = __shfl_sync(0xffffffffu, w_meta, k);
-      const uint32_t meta2 = __shfl_sync(0xffffffffu, w_meta, k2);
-      const int slot = issued % T::kSlots;
+      const uint32_t slot = issued % T::kSlots;
       if (lane == 0) {
         slot_start[slot] = start;
         slot_phys[slot] = start_p;
-        slot_meta[slot] = meta | (cand ? 4u | (((meta2 >> 4) & 31u) << 9) : 0u);
+        slot_meta[slot] = meta;
         // No proxy fence before the copy: every generic read of this ring
         // space has returned its value (consumed by the page math) already.
         const uint32_t bar = smem_u32(&bars[slot]);
         mbar_expect_tx(bar, need);
+        const bool pair = (meta & 4u) != 0;
+        const uint32_t rb = pair ? need >> 1 : need;
         bulk_g2s(smem_u32(ring + start_p), p.arena + src, rb, bar);
-        if (cand) bulk_g2s(smem_u32(ring + start_p + rb), p.arena + src2, rb, bar);
+        if (pair) bulk_g2s(smem_u32(ring + start_p + rb), p.arena + src2, rb, bar);
       }
       head = start + need;
       head_p = start_p + need;
       ++issued;
-      w_mask &= ~(kbit | (1u << k2));
+      w_mask &= w_mask - 1u;
     }
     __syncwarp();
     if (issued == consumed) break;
     // Consumer: the oldest record.
-    const int slot = consumed % T::kSlots;
-    if (!mbar_wait_bounded(smem_u32(&bars[slot]), (uint32_t)(consumed / T::kSlots) & 1u)) {
+    const uint32_t slot = consumed % T::kSlots;
+    if (!mbar_wait_bounded(smem_u32(&bars[slot]), (consumed / T::kSlots) & 1u)) {
       timed_out = true;
       break;
     }
@@ -706,7 +719,7 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
   if (timed_out) {
     if (lane == 0) set_status(p.status, AKV_DEV_TIMEOUT);
     // Let the copies still in flight land (bounded) before the warp exits.
-    for (int k = consumed; k < issued; ++k)
+    for (uint32_t k = consumed; k < issued; ++k)
       if (!mbar_wait_bounded(smem_u32(&bars[k % T::kSlots]), (uint32_t)(k / T::kSlots) & 1u)) break;
   }
   // Items past the last record (or with no visible page) still get a partial.
