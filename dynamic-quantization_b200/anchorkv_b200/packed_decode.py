@@ -18,41 +18,69 @@ accounting.  Differences in the physical plane:
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass
 
 import torch
 import torch.nn.functional as F
 
 from . import _lib
-from .pool import BLOCK, PagePool, encode, group_ok, record_bytes
+from .pool import BLOCK, PagePool, encode, group_ok, record_bytes, v_order
 
 
 def tensor_bytes(tensor) -> int:
     return tensor.numel() * tensor.element_size()
 
 
-@dataclass
 class QuantizedPage:
     """One page of K or V: ``[KV heads, 16, head dim]`` as fp16, int8 or packed int4.
 
-    ``data``/``scales`` may be views into a page pool (strided across heads).
-    ``nbytes`` counts payload + scales (packed_decode.py:28-32)."""
+    ``data`` is the row-major payload and ``scales`` the fp16 scales, as the
+    reference holds them; either may be a view into a page pool (strided
+    across heads).  A V page of a pool record stores its payload bytes in the
+    decode kernel's swizzled order (:func:`~anchorkv_b200.pool.v_swizzle`):
+    ``order`` is then the byte map, ``stored`` the record view, and ``data``
+    a row-major copy.  ``nbytes`` counts payload + scales
+    (packed_decode.py:28-32)."""
 
-    bits: int
-    data: torch.Tensor
-    scales: torch.Tensor | None
-    shape: tuple
-    group: int
+    def __init__(self, bits: int, data: torch.Tensor, scales: torch.Tensor | None, shape: tuple, group: int,
+                 *, order: torch.Tensor | None = None):
+        self.bits = bits
+        self.stored = data
+        self.scales = scales
+        self.shape = shape
+        self.group = group
+        self.order = order
+
+    @property
+    def data(self) -> torch.Tensor:
+        if self.order is None:
+            return self.stored
+        heads = self.stored.shape[0]
+        flat = self.stored.reshape(heads, -1).view(torch.uint8)
+        return flat[:, self.order].view(self.stored.dtype).view(self.stored.shape)
 
     @property
     def nbytes(self) -> int:
-        return tensor_bytes(self.data) + (tensor_bytes(self.scales) if self.scales is not None else 0)
+        return tensor_bytes(self.stored) + (tensor_bytes(self.scales) if self.scales is not None else 0)
+
+    def write_rows(self, start: int, rows: torch.Tensor) -> None:
+        """Store token rows ``[heads, n, dim]`` (fp16 pages) from ``start``."""
+        n = rows.shape[1]
+        if self.order is None:
+            self.stored[:, start:start + n].copy_(rows)
+            return
+        if self.bits != 16:
+            raise ValueError('token rows are written into FP16 pages only')
+        rb = self.shape[-1] * 2  # the swizzle keeps every fp16 row inside its own bytes
+        src = rows.to(torch.float16).contiguous().view(torch.uint8).reshape(rows.shape[0], n * rb)
+        idx = self.order[start * rb:(start + n) * rb] - start * rb
+        dst = self.stored.view(torch.uint8).view(self.stored.shape[0], -1)  # a view: writes reach the pool
+        dst[:, start * rb:(start + n) * rb] = src[:, idx]
 
     def dense(self) -> torch.Tensor:
         """fp16 values: ``fp16(int * float(scale))`` (packed_decode.py:34-45)."""
         if self.bits == 16:
             return self.data
-        _lib.require_cuda(self.data, "page payload")
+        _lib.require_cuda(self.stored, "page payload")
         payload = self.data.contiguous()
         scales = self.scales.contiguous()
         out = torch.empty(self.shape, dtype=torch.float16, device=payload.device)
@@ -142,7 +170,8 @@ class PagedLayer:
                 ns = BLOCK * self.dim // self.group
                 sraw = rec[:, 2 * pb + kv * 2 * ns:2 * pb + (kv + 1) * 2 * ns]
                 scales = sraw.view(torch.float16).view(self.heads, BLOCK, self.dim // self.group)
-            out.append(QuantizedPage(bits, data, scales, shape, self.group))
+            order = v_order(self.dim, bits, data.device) if kv == 1 else None
+            out.append(QuantizedPage(bits, data, scales, shape, self.group, order=order))
         return tuple(out)
 
     def _publish(self, page: int) -> None:
@@ -167,8 +196,8 @@ class PagedLayer:
                 self.pages.append(self._views(16, slot))
             take = min(self.block - position, key.shape[-2] - offset)
             kpage, vpage = self.pages[page]
-            kpage.data[:, position:position + take].copy_(key[0, :, offset:offset + take])
-            vpage.data[:, position:position + take].copy_(value[0, :, offset:offset + take])
+            kpage.write_rows(position, key[0, :, offset:offset + take])
+            vpage.write_rows(position, value[0, :, offset:offset + take])
             self.length += take
             offset += take
             self._publish(page)

@@ -3,10 +3,13 @@
 A page is 16 tokens of K and V for every KV head of one (sequence, layer).  It
 is stored as ``heads`` head records back to back; a head record is
 ``[K payload][V payload][K scales][V scales][pad to 16 B]`` with the reference
-byte layout for the payload (row-major fp16, int8, or two's-complement nibbles
-with the even element low, as ``packed_decode.pack_page`` writes them,
-packed_decode.py:48-67) and fp16 scales.  Pages live at 16-byte aligned
-offsets so one bulk copy moves a head record from HBM into shared memory.
+byte layout for the payload (fp16, int8, or two's-complement nibbles with the
+even element low, as ``packed_decode.pack_page`` writes them,
+packed_decode.py:48-67) and fp16 scales.  K payloads are row-major; V payloads
+hold the same bytes with 16-byte units permuted inside each 128-byte line
+(:func:`v_swizzle`), the order the decode kernel reads without shared-memory
+bank conflicts.  Pages live at 16-byte aligned offsets so one bulk copy moves a
+head record from HBM into shared memory.
 
 A page table entry (descriptor) is an int64: mode in bits 0-1 (0 = skip:
 evicted or not visible, 1 = INT4, 2 = INT8, 3 = FP16), valid tokens - 1 in
@@ -36,6 +39,42 @@ def record_bytes(dim: int, group: int, bits: int) -> int:
     payload = BLOCK * dim * bits // 8
     scales = 0 if bits == 16 else BLOCK * dim // group
     return (2 * payload + 4 * scales + 15) // 16 * 16
+
+
+def v_swizzle(dim: int, bits: int, offsets) -> np.ndarray:
+    """Stored byte offset of each row-major byte offset of a V payload, and
+    back (the map is an involution); mirrors ``v_swizzle`` in akv_common.cuh.
+
+    The 16-byte units of a V payload are permuted inside each 128-byte line by
+    an XOR keyed on the line's token row, so the decode kernel's V fragment
+    loads hit distinct shared-memory banks.  K payloads and scales are
+    row-major."""
+    o = np.asarray(offsets, np.int64)
+    row = dim * bits // 8
+    if row == 256:
+        key = ((o >> 9) & 1) | (((o >> 10) & 1) << 2)
+    elif row == 128:
+        key = (o >> 7) & 6
+    elif row == 64:
+        key = (o >> 6) & 6
+    elif row == 32:
+        key = (o >> 6) & 2
+    else:
+        raise ValueError(f"no V payload layout for head_dim {dim} at {bits} bits")
+    return o ^ (key << 4)
+
+
+_V_ORDER: dict = {}
+
+
+def v_order(dim: int, bits: int, device) -> torch.Tensor:
+    """int64 index over one V payload's bytes: ``stored[i] == row_major[order[i]]``
+    (and ``row_major[i] == stored[order[i]]``)."""
+    key = (dim, bits, str(device))
+    if key not in _V_ORDER:
+        n = BLOCK * dim * bits // 8
+        _V_ORDER[key] = torch.from_numpy(v_swizzle(dim, bits, np.arange(n))).to(device)
+    return _V_ORDER[key]
 
 
 def encode(bits: int | None, ntok: int, offset: int) -> int:

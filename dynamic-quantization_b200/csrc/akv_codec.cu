@@ -84,22 +84,24 @@ struct Slab {
 
 // Dequantize 8 consecutive elements of a record payload to fp16, exactly as
 // QuantizedPage.dense (packed_decode.py:34-45): fp16(int * float(scale)).
+// `vpay`: a V payload, stored in the swizzled byte order (v_swizzle).
 template <int D, int G>
 __device__ __forceinline__ uint4 record_load8(int mode, const uint8_t *payload, const __half *sc,
-                                              int c, int lane) {
+                                              int c, int lane, bool vpay) {
   const int e = 256 * c + 8 * lane;
-  if (mode == AKV_MODE_FP16) return *reinterpret_cast<const uint4 *>(payload + 2 * e);
+  auto at = [&](int64_t o) { return payload + (vpay ? v_swizzle(D, mode, o) : o); };
+  if (mode == AKV_MODE_FP16) return *reinterpret_cast<const uint4 *>(at(2 * e));
   const float s = __half2float(sc[e / G]);
   int q[8];
   if (mode == AKV_MODE_INT8) {
-    const uint2 w = *reinterpret_cast<const uint2 *>(payload + e);
+    const uint2 w = *reinterpret_cast<const uint2 *>(at(e));
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       q[i] = (int)(int8_t)(w.x >> (8 * i));
       q[4 + i] = (int)(int8_t)(w.y >> (8 * i));
     }
   } else {
-    const uint32_t w = *reinterpret_cast<const uint32_t *>(payload + e / 2);
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(at(e / 2));
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       int n = (w >> (4 * i)) & 15;
@@ -192,13 +194,17 @@ __device__ __forceinline__ void quantize_chunk(const uint4 &v, float s, float r,
 }
 
 // Quantize one slab held in registers (v[c] = 8 fp16 values) into a record.
+// `vpay`: a V payload, written in the swizzled byte order (v_swizzle); each
+// lane's 16, 8 or 4 bytes stay inside one 16-byte unit, and a warp's store
+// covers the same 128-byte lines as the row-major one.
 template <int D, int G, int SEM>
 __device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], int mode,
-                                           uint8_t *payload, __half *sc, int lane) {
+                                           uint8_t *payload, __half *sc, int lane, bool vpay) {
   constexpr int NC = Slab<D>::kChunks;
+  auto at = [&](int64_t o) { return payload + (vpay ? v_swizzle(D, mode, o) : o); };
   if (mode == AKV_MODE_FP16) {
 #pragma unroll
-    for (int c = 0; c < NC; ++c) *reinterpret_cast<uint4 *>(payload + 512 * c + 16 * lane) = v[c];
+    for (int c = 0; c < NC; ++c) *reinterpret_cast<uint4 *>(at(512 * c + 16 * lane)) = v[c];
     return;
   }
   const float qmax = mode == AKV_MODE_INT8 ? 127.f : 7.f;
@@ -243,12 +249,12 @@ __device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], i
     if (mode == AKV_MODE_INT8) {
       const uint32_t w0 = prmt(prmt(t[0], t[1], 0x0040u), prmt(t[2], t[3], 0x0040u), 0x5410u);
       const uint32_t w1 = prmt(prmt(t[4], t[5], 0x0040u), prmt(t[6], t[7], 0x0040u), 0x5410u);
-      *reinterpret_cast<uint2 *>(payload + e) = make_uint2(w0, w1);
+      *reinterpret_cast<uint2 *>(at(e)) = make_uint2(w0, w1);
     } else {
       uint32_t pb[4];  // byte k: element 2k in the low nibble, 2k+1 in the high nibble
 #pragma unroll
       for (int k = 0; k < 4; ++k) pb[k] = (t[2 * k] & 0x0fu) | ((t[2 * k + 1] << 4) & 0xf0u);
-      *reinterpret_cast<uint32_t *>(payload + e / 2) =
+      *reinterpret_cast<uint32_t *>(at(e / 2)) =
           prmt(prmt(pb[0], pb[1], 0x0040u), prmt(pb[2], pb[3], 0x0040u), 0x5410u);
     }
     if (e % G == 0) sc[e / G] = gs.stored;
@@ -301,7 +307,7 @@ __global__ void __launch_bounds__(256, 3) pack_pages_kernel(
       const __half *sc =
           reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, smode);
 #pragma unroll
-      for (int c = 0; c < NC; ++c) v[c] = record_load8<D, G>(smode, pay, sc, c, lane);
+      for (int c = 0; c < NC; ++c) v[c] = record_load8<D, G>(smode, pay, sc, c, lane, kv == 1);
     } else {
       const __half *src = (kv ? src_v : src_k) + (p / blocks_per_row) * outer_stride +
                           h * head_stride + (p % blocks_per_row) * (int64_t)kBlock * D;
@@ -313,7 +319,7 @@ __global__ void __launch_bounds__(256, 3) pack_pages_kernel(
     const int64_t pb = payload_bytes(D, dmode);
     const int64_t ns = scale_count(D, G, dmode);
     __half *sc = reinterpret_cast<__half *>(rec + 2 * pb) + kv * ns;
-    store_slab<D, G, SEM>(v, dmode, rec + kv * pb, sc, lane);
+    store_slab<D, G, SEM>(v, dmode, rec + kv * pb, sc, lane, kv == 1);
     if (kv == 1) {  // zero the record's alignment pad so records are deterministic
       const int64_t used = 2 * pb + 4 * ns;
       if (lane < drec - used) rec[used + lane] = 0;
@@ -351,7 +357,7 @@ __global__ void __launch_bounds__(256) unpack_pages_kernel(const int64_t *__rest
         const uint8_t *rec = arena + desc_offset(d) + h * rb;
         const int64_t pb = payload_bytes(D, mode);
         const __half *sc = reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, mode);
-        v = record_load8<D, G>(mode, rec + kv * pb, sc, c, lane);
+        v = record_load8<D, G>(mode, rec + kv * pb, sc, c, lane, kv == 1);
       }
       *reinterpret_cast<uint4 *>(out + 256 * c + 8 * lane) = v;
     }

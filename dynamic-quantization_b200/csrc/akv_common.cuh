@@ -40,6 +40,24 @@ __host__ __device__ inline int64_t record_bytes(int D, int group, int mode) {
   return (b + 15) & ~(int64_t)15;
 }
 
+// V payload byte order.  The 16-byte units of a V payload are permuted inside
+// each 128-byte line: unit u of the line holding token row r is stored at
+// u ^ S(r), with S chosen per row width (D * bits / 8 bytes) so that the
+// decode's V fragment loads (lane (g, t) reads row 2t + {0, 1, 8, 9} at column
+// g) land in 32 distinct banks.  S depends only on the line, so the map is an
+// involution: the same function converts stored <-> row-major offsets.  K
+// payloads and all scales stay row-major.
+__host__ __device__ constexpr int v_swizzle_key(int row_bytes, int64_t o) {
+  return row_bytes == 256   ? (int)(((o >> 9) & 1) | (((o >> 10) & 1) << 2))  // t = row/2 mod 4 -> {0,1,4,5}
+         : row_bytes == 128 ? (int)((o >> 7) & 6)                              // row & 6
+         : row_bytes == 64  ? (int)((o >> 6) & 6)                              // row & 6 (two rows per line)
+                            : (int)((o >> 6) & 2);                             // (row >> 1) & 2 (four rows per line)
+}
+// Stored offset of row-major byte offset `o` of a V payload (and vice versa).
+__host__ __device__ constexpr int64_t v_swizzle(int D, int mode, int64_t o) {
+  return mode == AKV_MODE_SKIP ? o : o ^ ((int64_t)v_swizzle_key(D * mode_bits(mode) / 8, o) << 4);
+}
+
 // ------------------------------------------------------------------ PTX: sync
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);

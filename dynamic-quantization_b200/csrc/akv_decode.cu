@@ -221,7 +221,13 @@ __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, 
   constexpr int PARTS = W >= 8 ? 2 : 1;       // load wide slices in halves (fewer live registers)
   constexpr int WP = W / PARTS;
   constexpr int TP = (D / 16) / PARTS;        // m-tiles per part
-  const uint8_t *base = vrec + gid * (W * 4);
+  // Stored offsets of the lane's row slices in the swizzled V payload
+  // (v_swizzle): row 2t4 is c0; the second half of a 32-byte slice flips bit
+  // 4; row 2t4+1 flips the row bit of a line holding two or four rows, or is
+  // one row further; rows +8 are 8 rows further.  Within each phase of the
+  // shared-memory load the lanes hit distinct banks.
+  const int c0 = (int)v_swizzle(D, MODE, (2 * t4) * rowB + gid * (W * 4));
+  constexpr int kOddRow = rowB == 64 ? 64 : (rowB == 32 ? 32 : 0);
   auto sc = [](uint32_t x, uint32_t s) { return FOLD ? x : hmul2(x, s); };
   uint32_t sab = 0, scd = 0;
   if constexpr (MODE != AKV_MODE_FP16 && !FOLD) {
@@ -235,10 +241,13 @@ __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, 
 #pragma unroll
   for (int part = 0; part < PARTS; ++part) {
     uint32_t wa[WP], wb[WP], wc[WP], wd[WP];
-    lds_words<WP>(base + (2 * t4) * rowB + 4 * WP * part, wa);
-    lds_words<WP>(base + (2 * t4 + 1) * rowB + 4 * WP * part, wb);
-    lds_words<WP>(base + (2 * t4 + 8) * rowB + 4 * WP * part, wc);
-    lds_words<WP>(base + (2 * t4 + 9) * rowB + 4 * WP * part, wd);
+    static_assert(PARTS == 1 || 4 * WP == 16, "a slice half is one 16-byte unit");
+    const int ca = c0 ^ (16 * part);
+    const int cb = kOddRow ? (ca ^ kOddRow) : ca + rowB;
+    lds_words<WP>(vrec + ca, wa);
+    lds_words<WP>(vrec + cb, wb);
+    lds_words<WP>(vrec + ca + 8 * rowB, wc);
+    lds_words<WP>(vrec + cb + 8 * rowB, wd);
     float(&op)[TP][4] = *reinterpret_cast<float(*)[TP][4]>(&o[TP * part][0]);
     if constexpr (MODE == AKV_MODE_INT4) {
 #pragma unroll
@@ -330,13 +339,16 @@ __device__ __forceinline__ void pages_softmax(float (&s)[NP][4], const int (&nto
 }
 
 // Zero the V rows past a partial page's valid count, so that P = 0 never meets
-// a non-finite value.
+// a non-finite value.  The V payload is swizzled inside 128-byte lines, which
+// may hold several rows: every word from the line of row `ntok` on is zeroed
+// when the row it stores (v_swizzle maps stored to row-major offsets) is past
+// the count.
 template <int D, int MODE>
 __device__ __forceinline__ void zero_tail(uint8_t *rec, int ntok, int lane) {
   constexpr int PB = kBlock * D * mode_bits(MODE) / 8;
   constexpr int rowB = D * mode_bits(MODE) / 8;
-  for (int off = ntok * rowB + 4 * lane; off < PB; off += 128)
-    *reinterpret_cast<uint32_t *>(rec + PB + off) = 0u;
+  for (int off = ((ntok * rowB) & ~127) + 4 * lane; off < PB; off += 128)
+    if ((int)v_swizzle(D, MODE, off) >= ntok * rowB) *reinterpret_cast<uint32_t *>(rec + PB + off) = 0u;
 }
 
 // One FP16 page.

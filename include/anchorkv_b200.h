@@ -18,9 +18,16 @@
  *   - the page holds `heads` head records back to back, each
  *     akv_record_bytes(head_dim, group, mode) bytes:
  *       [K payload][V payload][K scales][V scales][zero pad to 16 bytes]
- *     payload = 16 rows x head_dim, row-major, fp16 / int8 / two's-complement
- *     nibbles with the even element in the low nibble (the reference byte
- *     layout); scales = fp16, element (row, col) uses scale (row*head_dim+col)/group;
+ *     payload = 16 rows x head_dim, fp16 / int8 / two's-complement nibbles
+ *     with the even element in the low nibble (the reference byte layout).
+ *     K payloads are row-major.  V payloads hold the same bytes with their
+ *     16-byte units permuted inside each 128-byte line: row-major offset o is
+ *     stored at o ^ (key << 4), where, for token row r and row width
+ *     w = head_dim * bits / 8, key = r & 6 (w = 128 or 64), (r >> 1) & 2
+ *     (w = 32), or t&1 | (t&2) << 1 with t = (r >> 1) & 3 (w = 256).  The
+ *     map is its own inverse.  It makes the decode's V fragment loads free
+ *     of shared-memory bank conflicts;
+ *     scales = fp16, element (row, col) uses scale (row*head_dim+col)/group;
  *   - a page descriptor is an int64:
  *       bits 0-1  mode (AKV_MODE_*; AKV_MODE_SKIP = evicted or not visible)
  *       bits 2-5  valid tokens in the page minus one (0..15)

@@ -44,9 +44,32 @@ def slab_payload(slab: np.ndarray, bits: int, group: int, semantics: str):
     return np.asarray(payload).tobytes(), np.asarray(scales, np.float16).tobytes()
 
 
+def v_stored(payload: bytes, dim: int, bits: int) -> bytes:
+    """A row-major V payload in the pool's stored order: the 16-byte unit u of
+    the 128-byte line that holds token row r is stored at unit u ^ key(r),
+    key chosen per row width so the decode's V fragment loads are free of
+    bank conflicts."""
+    row = dim * bits // 8
+    src = np.frombuffer(payload, np.uint8).reshape(-1, 16)  # 16-byte units
+    out = np.empty_like(src)
+    for u in range(src.shape[0]):
+        r = 16 * u // row
+        if row == 256:
+            t = (r >> 1) & 3
+            key = (t & 1) | ((t & 2) << 1)
+        elif row in (128, 64):
+            key = r & 6
+        else:
+            key = (r >> 1) & 2
+        line, unit = divmod(u, 8)
+        out[8 * line + (unit ^ key)] = src[u]
+    return out.tobytes()
+
+
 def record_bytes_expected(kslab, vslab, bits, group, semantics, record_size) -> bytes:
     kp, ks = slab_payload(kslab, bits, group, semantics)
     vp, vs = slab_payload(vslab, bits, group, semantics)
+    vp = v_stored(vp, np.asarray(vslab).shape[-1], bits)
     rec = kp + vp + ks + vs
     return rec + b"\0" * (record_size - len(rec))
 

@@ -38,6 +38,61 @@ def test_record_sizes_are_reference_bytes_plus_pad():
     assert P.record_bytes(128, 64, 16) == 8192
 
 
+def _bank_ways(addrs, width):
+    """Worst bank conflict of one shared-memory load: lanes are served in
+    phases of 128 / width lanes; equal addresses broadcast."""
+    per, worst = 128 // width, 1
+    for ph in range(32 // per):
+        banks = {}
+        for x in set(addrs[ph * per:(ph + 1) * per]):
+            for w in range(width // 4):
+                banks.setdefault((x // 4 + w) % 32, set()).add(x // 128)
+        worst = max(worst, max(len(v) for v in banks.values()))
+    return worst
+
+
+@pytest.mark.parametrize("dim", [64, 128])
+@pytest.mark.parametrize("bits", [4, 8, 16])
+def test_v_payload_order_is_line_local_involution_without_bank_conflicts(dim, bits):
+    from paged_reference import v_stored
+    n = 16 * dim * bits // 8
+    o = np.arange(n)
+    s = P.v_swizzle(dim, bits, o)
+    assert (np.sort(s) == o).all() and (s // 128 == o // 128).all()
+    assert (P.v_swizzle(dim, bits, s) == o).all()
+    logical = (np.arange(n) * 7 % 251).astype(np.uint8)
+    assert v_stored(logical.tobytes(), dim, bits) == logical[s].tobytes()
+    # The decode's V fragment loads: lane (g, t) reads token rows 2t, 2t+1,
+    # 2t+8, 2t+9 at its dim slice g (dim / 8 dims; 32-byte slices in halves).
+    row, slice_bytes = dim * bits // 8, dim // 8 * bits // 8
+    width = min(slice_bytes, 16)
+    linear, stored = [], []
+    for half in range(slice_bytes // width):
+        for dr in (0, 1, 8, 9):
+            a = [(2 * (ln & 3) + dr) * row + (ln >> 2) * slice_bytes + width * half for ln in range(32)]
+            linear.append(_bank_ways(a, width))
+            stored.append(_bank_ways(list(P.v_swizzle(dim, bits, a)), width))
+    assert max(linear) >= 2 and max(stored) == 1
+
+
+def test_pooled_v_page_rows_round_trip_through_the_stored_order():
+    from anchorkv_b200.packed_decode import QuantizedPage
+    from paged_reference import v_stored
+    heads, dim = 2, 128
+    rec = torch.zeros(heads, 16 * dim * 2 + 48, dtype=torch.uint8)  # strided like a pool record view
+    view = rec[:, :16 * dim * 2].view(torch.float16).view(heads, 16, dim)
+    page = QuantizedPage(16, view, None, (heads, 16, dim), 64, order=P.v_order(dim, 16, "cpu"))
+    rows = torch.randn(heads, 5, dim).half()
+    page.write_rows(3, rows)
+    page.write_rows(8, rows[:, :2])
+    want = torch.zeros(heads, 16, dim, dtype=torch.float16)
+    want[:, 3:8], want[:, 8:10] = rows, rows[:, :2]
+    assert torch.equal(page.data, want)
+    for h in range(heads):
+        assert rec[h, :16 * dim * 2].numpy().tobytes() == v_stored(want[h].numpy().tobytes(), dim, 16)
+    assert (rec[:, 16 * dim * 2:] == 0).all()
+
+
 def test_parser_matches_reference_behaviour():
     parser = akv.DeclarativeAttentionParser()
     assert parser.feed("reason <fo") == ()
