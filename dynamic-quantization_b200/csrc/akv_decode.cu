@@ -48,18 +48,26 @@
 
 namespace akv {
 
+// One CTA per SM, holding all of the SM's streaming warps (16 at 128
+// registers).  The warp schedulers favour older CTAs: with four 4-warp CTAs
+// per SM the youngest CTA's warps finished about 15 % after the oldest's on
+// equal work, and that spread was the decode's tail.  Warps of one CTA share
+// one age and finish together.  Small problems launch fewer warps per CTA so
+// that every CTA still has an SM of its own.
 template <int D>
 struct DecodeTraits {
-  static constexpr int kWarps = 4;     // independent streaming warps per CTA
-  static constexpr int kThreads = kWarps * 32;
-  static constexpr int kCtasPerSm = 4;   // 16 warps per SM (128 registers, 53 KB smem per CTA)
-  static constexpr int kRing = 13312;  // bytes of ring per warp (3 INT4 page pairs)
-  static constexpr int kSlots = 8;     // records in flight per warp
-  static constexpr int DK = D / 4;     // K dims a lane owns per row
-  static constexpr int DV = D / 8;     // V dims a lane owns per row
+  static constexpr int kMaxWarps = 16;  // independent streaming warps per CTA, at most
+  static constexpr int kMaxThreads = kMaxWarps * 32;
+  static constexpr int kRing = 13312;   // bytes of ring per warp (3 INT4 page pairs)
+  static constexpr int kSlots = 8;      // records in flight per warp
+  static constexpr int DK = D / 4;      // K dims a lane owns per row
+  static constexpr int DV = D / 8;      // V dims a lane owns per row
   static constexpr int kTiles = D / 16;
-  static constexpr int kSmem = kWarps * kRing + kWarps * kSlots * (8 + 4 + 4 + 4);
-  static_assert(kRing % 16 == 0 && kRing >= 4 * kBlock * D, "a ring must hold one FP16 record");
+  // A warp's shared memory: its ring, then its slot barriers and records.
+  static constexpr int kWarpBytes = kRing + kSlots * (8 + 4 + 4 + 4);
+  static constexpr int kSmemMax = kMaxWarps * kWarpBytes;
+  static_assert(kRing % 16 == 0 && kWarpBytes % 16 == 0, "rings stay 16-byte aligned");
+  static_assert(kRing >= 4 * kBlock * D, "a ring must hold one FP16 record");
   // Two INT8 records with the finest scale group (32) form the largest pair.
   static_assert(kRing >= 2 * (2 * kBlock * D + 2 * (kBlock * D / 32) * 2 + 16), "a ring must hold a pair");
 };
@@ -462,7 +470,7 @@ __device__ __forceinline__ void query_fragments(const uint32_t (&qw)[D / 8], uin
 // SLAB: one scale per 16-token slab (group = 16 * head_dim), the
 // per-block-per-KV-head layout; false: per-row groups (32/64/128).
 template <int D, bool SLAB>
-__global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kCtasPerSm)
+__global__ void __launch_bounds__(DecodeTraits<D>::kMaxThreads, 1)
     decode_streamk_kernel(const DecodeParams p) {
   using T = DecodeTraits<D>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -483,7 +491,7 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
     h[kPartialsF] = (int32_t)((reinterpret_cast<const uint8_t *>(p.partials) -
                                reinterpret_cast<const uint8_t *>(p.header)) / 4);
   }
-  const int gw = blockIdx.x * T::kWarps + warp;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + warp;  // warps per CTA are chosen at launch
   const int mb = p.max_blocks;
   const int total = p.items * mb;
   const int e_begin = gw * p.range;
@@ -492,12 +500,11 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kThreads, DecodeTraits<D>::kC
   const int first_item = e_begin / mb, last_seg = (e_end - 1) / mb - first_item;
   const int ipb = p.kv_heads * p.qgroups;
 
-  uint8_t *ring = smem + warp * T::kRing;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + T::kWarps * T::kRing) + warp * T::kSlots;
-  uint32_t *slot_start = reinterpret_cast<uint32_t *>(smem + T::kWarps * T::kRing +
-                                                      T::kWarps * T::kSlots * 8) + warp * T::kSlots;
-  uint32_t *slot_meta = slot_start + T::kWarps * T::kSlots;
-  uint32_t *slot_phys = slot_meta + T::kWarps * T::kSlots;
+  uint8_t *ring = smem + warp * T::kWarpBytes;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(ring + T::kRing);
+  uint32_t *slot_start = reinterpret_cast<uint32_t *>(ring + T::kRing + T::kSlots * 8);
+  uint32_t *slot_meta = slot_start + T::kSlots;
+  uint32_t *slot_phys = slot_meta + T::kSlots;
 
   const int lg = p.log2_group;
   ScaleIdx si;
@@ -1080,30 +1087,31 @@ __global__ void __launch_bounds__(D) merge_states_kernel(const float *__restrict
 
 // ------------------------------------------------------------------- host
 struct Plan {
-  int warps, range, smax, slot_heads, items, qgroups, ctas;
+  int warps, range, smax, slot_heads, items, qgroups, ctas, wpc;  // wpc: warps per CTA
   int64_t bytes;
 };
 
+// CTAs of kMaxWarps warps the device holds at once (one per SM).
 template <int D>
-static int device_warps(int *out) {
+static int device_ctas(int *out) {
   using T = DecodeTraits<D>;
   int dev = 0, sms = 0, per_sm = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return AKV_ERR_CUDA;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return AKV_ERR_CUDA;
   int per_sm_slab = 0;
   if (cudaFuncSetAttribute(decode_streamk_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           T::kSmem) != cudaSuccess ||
+                           T::kSmemMax) != cudaSuccess ||
       cudaFuncSetAttribute(decode_streamk_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           T::kSmem) != cudaSuccess)
+                           T::kSmemMax) != cudaSuccess)
     return AKV_ERR_CUDA;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_streamk_kernel<D, false>, T::kThreads,
-                                                    T::kSmem) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_streamk_kernel<D, false>, T::kMaxThreads,
+                                                    T::kSmemMax) != cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_slab, decode_streamk_kernel<D, true>,
-                                                    T::kThreads, T::kSmem) != cudaSuccess)
+                                                    T::kMaxThreads, T::kSmemMax) != cudaSuccess)
     return AKV_ERR_CUDA;
   per_sm = std::min(per_sm, per_sm_slab);  // both variants get the same decomposition
   if (per_sm < 1) return AKV_ERR_CUDA;
-  *out = sms * per_sm * T::kWarps;
+  *out = sms * per_sm;
   return AKV_OK;
 }
 
@@ -1120,10 +1128,12 @@ static int make_plan(int batch, int q_heads, int kv_heads, int head_dim, int max
   const int64_t total = items * max_blocks;
   if (items > (1 << 30) || total >= (1ll << 31)) return AKV_ERR_UNSUPPORTED;
   pl.items = (int)items;
-  int dev_warps = 0;
-  const int st = head_dim == 64 ? device_warps<64>(&dev_warps) : device_warps<128>(&dev_warps);
+  int dev_ctas = 0;
+  const int st = head_dim == 64 ? device_ctas<64>(&dev_ctas) : device_ctas<128>(&dev_ctas);
   if (st != AKV_OK) return st;
-  int64_t warps = dev_warps;
+  constexpr int kMaxWarps = DecodeTraits<128>::kMaxWarps;
+  static_assert(DecodeTraits<64>::kMaxWarps == kMaxWarps, "one decomposition for both head dims");
+  int64_t warps = (int64_t)dev_ctas * kMaxWarps;
   if (splits > 0) warps = std::min<int64_t>(warps, items * (int64_t)splits);
   warps = std::max<int64_t>(1, std::min<int64_t>(warps, std::max<int64_t>(total, 1)));
   const int64_t range = std::max<int64_t>(1, (total + warps - 1) / warps);
@@ -1131,7 +1141,9 @@ static int make_plan(int batch, int q_heads, int kv_heads, int head_dim, int max
   pl.range = (int)range;
   pl.warps = (int)warps;
   pl.smax = max_blocks > 0 ? (int)(1 + (range - 1 + max_blocks - 1) / max_blocks) : 1;
-  pl.ctas = (int)((warps + DecodeTraits<128>::kWarps - 1) / DecodeTraits<128>::kWarps);
+  // One CTA per SM: spread fewer warps over as many SMs as they can use.
+  pl.wpc = (int)std::min<int64_t>(kMaxWarps, (warps + dev_ctas - 1) / dev_ctas);
+  pl.ctas = (int)((warps + pl.wpc - 1) / pl.wpc);
   pl.bytes = kHeaderBytes + (int64_t)pl.warps * pl.smax * pl.slot_heads * (head_dim + 4) * 4;
   *plan = pl;
   return AKV_OK;
@@ -1219,10 +1231,10 @@ static int decode_launch(const void *arena, int64_t arena_bytes, const int64_t *
   cudaError_t err;
   if (head_dim == 64)
     err = launch_dependent(slab ? decode_streamk_kernel<64, true> : decode_streamk_kernel<64, false>, pl.ctas,
-                           DecodeTraits<64>::kThreads, DecodeTraits<64>::kSmem, s, p);
+                           pl.wpc * 32, pl.wpc * DecodeTraits<64>::kWarpBytes, s, p);
   else
     err = launch_dependent(slab ? decode_streamk_kernel<128, true> : decode_streamk_kernel<128, false>, pl.ctas,
-                           DecodeTraits<128>::kThreads, DecodeTraits<128>::kSmem, s, p);
+                           pl.wpc * 32, pl.wpc * DecodeTraits<128>::kWarpBytes, s, p);
   return err == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
 }
 
