@@ -327,12 +327,28 @@ def run_ours(args, wl):
     q_host = q.cpu().pin_memory()
     out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     q_dev = torch.empty_like(q)
+    copies = torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event() for _ in range(L)]
+    ev_out = [torch.cuda.Event() for _ in range(L)]
 
     def e2e_step():
-        q_dev.copy_(q_host, non_blocking=True)
+        # Every layer's query goes in from pinned memory on a copy stream while
+        # the layers before it decode, and its output comes back as soon as its
+        # merge has run; the step ends when the last output is on the host.
+        copies.wait_stream(stream)  # the previous step is done with q_dev
+        with torch.cuda.stream(copies):
+            for l in range(L):
+                q_dev[l].copy_(q_host[l], non_blocking=True)
+                ev_in[l].record(copies)
         for l in range(L):
+            stream.wait_event(ev_in[l])
             akv.packed_attention(q_dev[l], layers[l], scale, splits=splits, out=out[l])
-        out_host.copy_(out, non_blocking=True)
+            ev_out[l].record(stream)
+        with torch.cuda.stream(copies):
+            for l in range(L):
+                copies.wait_event(ev_out[l])
+                out_host[l].copy_(out[l], non_blocking=True)
+        stream.wait_stream(copies)
 
     for _ in range(max(3, args.warmup)):
         e2e_step()
@@ -386,7 +402,8 @@ def run_ours(args, wl):
             "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4), "tokens_per_s": round(B * world / (e2e_ms * 1e-3), 1),
                     "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2,
-                    "path": "anchorkv_b200.packed_attention per layer, pinned host queries/outputs"},
+                    "path": "anchorkv_b200.packed_attention per layer; per-layer query/output copies from/to "
+                            "pinned host memory on a copy stream, overlapping the other layers' decode"},
             "gpu_launches": args.steps * L * 2,
             "clocks": clocks,
         }
