@@ -2,6 +2,7 @@
 """Benchmark of the packed mixed-precision KV decode path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload batched]
+    python bench.py --impl reference_gpu   # the reference's own Triton decode beside ours (batch 1)
 
 A step is one decode token for every sequence of the batch through all layers:
 per layer, the paged split-K decode kernel and the LSE merge kernel over that
@@ -19,6 +20,11 @@ device time per step); the KV pool (25.6 GB per GPU) is far larger than L2,
 so every step reads HBM.  e2e: the same metric through the public Python
 entry point with the step's queries copied from pinned host memory and the
 outputs read back inside the timed region.
+
+--impl reference times the reference's PyTorch CPU path (the reference arm);
+--impl reference_gpu runs the reference's own GPU decode (its Triton kernel,
+installed unmodified in baseline/_ref) and ours on the same pages, at the
+batch-1, group-64 shapes that kernel supports.
 """
 
 from __future__ import annotations
@@ -759,18 +765,101 @@ def run_reference(args, wl):
     print(json.dumps(line), flush=True)
 
 
+# Batch-1 shapes the reference's packed GPU kernel takes (group 64, head_dim 128):
+# (query heads, KV heads, context tokens).
+REF_GPU_CASES = [(16, 8, 512), (16, 8, 8192), (32, 8, 32768)]
+
+
+def run_reference_gpu(args):
+    """The reference's own GPU decode next to ours, one JSON line per case.
+
+    The reference, installed unmodified in baseline/_ref, builds its PagedLayer
+    (packed_decode.py:108-194) and runs its Triton packed_attention
+    (triton_decode.py:85-104, default splits=4); ours builds
+    anchorkv_b200.PagedLayer from the same appended K/V and runs
+    anchorkv_b200.packed_attention with the same arguments.  Pages older than
+    the two most recent are archived to INT4 by both.  Each call is timed with
+    CUDA events over --steps calls after --warmup; bytes are the resident
+    payload + scales of the layer."""
+    import torch
+
+    ref_dir = ROOT / "baseline" / "_ref"
+    sys.path.insert(0, str(ref_dir))
+    try:
+        from anchorkv import packed_decode as ref_pd
+        from anchorkv import triton_decode as ref_td
+    except Exception as exc:  # not installed, or its dependencies are missing
+        print(json.dumps({"impl": "reference_gpu", "unavailable": f"reference not importable from {ref_dir}: "
+                                                                     f"{type(exc).__name__}: {exc}"}), flush=True)
+        return
+    import anchorkv_b200 as akv
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    D, group = 128, 64
+    for hq, hkv, tokens in REF_GPU_CASES:
+        gen = torch.Generator(device=dev).manual_seed(tokens + hq)
+        k = torch.randn((1, hkv, tokens, D), generator=gen, device=dev).half()
+        v = torch.randn((1, hkv, tokens, D), generator=gen, device=dev).half()
+        q = torch.randn((1, hq, 1, D), generator=gen, device=dev).half()
+        scale = D ** -0.5
+        ref = ref_pd.PagedLayer(hkv, D, tokens, group=group, archive_bits=4, recent_pages=2, device=dev)
+        ours = akv.PagedLayer(hkv, D, tokens, group=group, archive_bits=4, recent_pages=2, device=dev)
+        for begin in range(0, tokens, 256):
+            ref.append(k[:, :, begin:begin + 256], v[:, :, begin:begin + 256])
+            ours.append(k[:, :, begin:begin + 256], v[:, :, begin:begin + 256])
+        assert [p[0].bits for p in ref.pages] == [p[0].bits for p in ours.pages]
+
+        def timed(fn):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize(dev)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(args.steps):
+                fn()
+            b.record()
+            torch.cuda.synchronize(dev)
+            return a.elapsed_time(b) / args.steps
+
+        out_ref = ref_td.packed_attention(q, ref, scale)
+        out_ours = akv.packed_attention(q, ours, scale)
+        diff = float((out_ref.float() - out_ours.float()).abs().max())
+        ms_ref = timed(lambda: ref_td.packed_attention(q, ref, scale))
+        ms_ours = timed(lambda: akv.packed_attention(q, ours, scale))
+        assert akv.take_device_status(dev) == 0
+        nbytes = ours.payload_bytes
+        line = {
+            "impl": "reference_gpu", "metric": "batch-1 decode-attn resident-KV GB/s, the reference's Triton "
+                                              "packed_attention and ours on the same pages",
+            "unit": "GB/s", "higher_is_better": True, "steps": args.steps, "warmup": args.warmup,
+            "config": {"workload": f"one sequence, {tokens} tokens, {hq} query / {hkv} KV heads, head_dim {D}, "
+                                   f"group {group}, pages older than the last two archived to INT4",
+                       "splits": 4, "resident_bytes": nbytes, "pages": len(ours.pages)},
+            "reference": {"ms_per_call": round(ms_ref, 5), "value": round(nbytes / (ms_ref * 1e-3) / 1e9, 2)},
+            "ours": {"ms_per_call": round(ms_ours, 5), "value": round(nbytes / (ms_ours * 1e-3) / 1e9, 2)},
+            "max_abs_diff": diff,
+        }
+        print(json.dumps(line), flush=True)
+        del ref, ours, k, v
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--impl", choices=("ours", "reference", "reference_gpu"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["long", "pack", "pack_small"], default="batched")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
+    if args.impl == "reference_gpu":
+        run_reference_gpu(args)
+        return
     if args.workload in ("pack", "pack_small"):
         if args.impl == "reference":
             cb = pack_cpu_baseline(args.cpu_seconds)

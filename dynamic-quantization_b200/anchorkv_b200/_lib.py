@@ -125,11 +125,17 @@ _status = {}
 
 def status_word(device):
     """The per-device int32 word kernels OR their error bits into."""
+    word = _status.get(device)  # fast path: the device object seen before
+    if word is not None:
+        return word
     import torch
 
-    key = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
+    dev = torch.device(device)
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
     if key not in _status:
         _status[key] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key))
+    if dev.index is not None:  # "cuda" without an index follows the current device: not cached by name
+        _status[device] = _status[key]
     return _status[key]
 
 

@@ -45,9 +45,10 @@ def packed_attention(query, layer, scale, splits=4, *, out=None):
     """Attend one query token per sequence over the layer's packed pages.
 
     ``query``: fp16 CUDA ``[batch, Hq, 1, D]`` (batch 1 for a PagedLayer).
-    ``splits``: at most this many pieces per (sequence, KV head), merged by
-    LSE (the reference's split-K knob; ``0`` lets the device use every resident
-    warp).  Results do not depend on it beyond fp32 rounding.
+    ``splits``: at least this many pieces per (sequence, KV head), merged by
+    LSE (the reference's split-K knob); the decode cuts finer, down to 16 pages
+    a piece, while the device has resident warps to spare (``0``: every
+    resident warp).  Results do not depend on it beyond fp32 rounding.
     """
     batched = isinstance(layer, PagedBatch)
     batch = layer.batch if batched else 1

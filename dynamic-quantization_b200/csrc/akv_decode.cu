@@ -42,6 +42,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "akv_common.cuh"
@@ -1090,13 +1091,28 @@ struct Plan {
   int warps, range, smax, slot_heads, items, qgroups, ctas, wpc;  // wpc: warps per CTA
   int64_t bytes;
 };
+// Finest cut of the work the decode makes on its own: entries (pages of one
+// item) a warp gets at least, against its fixed cost (query load, copy
+// pipeline fill, partial write, one more merge contributor).
+constexpr int64_t kMinPagesPerWarp = 16;
 
-// CTAs of kMaxWarps warps the device holds at once (one per SM).
+// CTAs of kMaxWarps warps the device holds at once (one per SM).  Constant per
+// device, so it is worked out (and the kernels' shared-memory limit raised)
+// once per device; later calls pay no CUDA queries for it.
 template <int D>
 static int device_ctas(int *out) {
   using T = DecodeTraits<D>;
+  static std::atomic<int> cached[256];  // per device ordinal, 0 until worked out
   int dev = 0, sms = 0, per_sm = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return AKV_ERR_CUDA;
+  const bool cacheable = dev >= 0 && dev < 256;
+  if (cacheable) {
+    const int c = cached[dev].load(std::memory_order_acquire);
+    if (c > 0) {
+      *out = c;
+      return AKV_OK;
+    }
+  }
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return AKV_ERR_CUDA;
   int per_sm_slab = 0;
   if (cudaFuncSetAttribute(decode_streamk_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1112,6 +1128,7 @@ static int device_ctas(int *out) {
   per_sm = std::min(per_sm, per_sm_slab);  // both variants get the same decomposition
   if (per_sm < 1) return AKV_ERR_CUDA;
   *out = sms * per_sm;
+  if (cacheable) cached[dev].store(sms * per_sm, std::memory_order_release);
   return AKV_OK;
 }
 
@@ -1134,7 +1151,11 @@ static int make_plan(int batch, int q_heads, int kv_heads, int head_dim, int max
   constexpr int kMaxWarps = DecodeTraits<128>::kMaxWarps;
   static_assert(DecodeTraits<64>::kMaxWarps == kMaxWarps, "one decomposition for both head dims");
   int64_t warps = (int64_t)dev_ctas * kMaxWarps;
-  if (splits > 0) warps = std::min<int64_t>(warps, items * (int64_t)splits);
+  // splits > 0: at least that many pieces per item, and finer cuts (down to
+  // kMinPagesPerWarp entries a warp) while the device has warps to spare.
+  if (splits > 0)
+    warps = std::min<int64_t>(warps, std::max<int64_t>(items * (int64_t)splits,
+                                                       (total + kMinPagesPerWarp - 1) / kMinPagesPerWarp));
   warps = std::max<int64_t>(1, std::min<int64_t>(warps, std::max<int64_t>(total, 1)));
   const int64_t range = std::max<int64_t>(1, (total + warps - 1) / warps);
   warps = std::max<int64_t>(1, (total + range - 1) / range);

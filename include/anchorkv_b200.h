@@ -134,9 +134,12 @@ int64_t akv_workspace_bytes(int batch, int q_heads, int kv_heads, int head_dim, 
  *   seq_blocks: per-sequence page count (NULL: every sequence has max_blocks);
  *   query: fp16 [batch][q_heads][head_dim] with the given strides (elements);
  *   q head h attends KV head h / (q_heads / kv_heads);
- *   splits: pieces each (sequence, KV head) is cut into at most (<= 0: as many
- *   as the device has resident warps); the kernel is persistent and gives
- *   every warp one contiguous range of (sequence, KV head, page) work.
+ *   splits: pieces each (sequence, KV head) is cut into at least, where it has
+ *   the pages (the reference's split-K count); the decode cuts finer, down to
+ *   16 pages a piece, while the device has resident warps to spare (<= 0: as
+ *   many pieces as the device has resident warps).  Results do not depend on
+ *   it beyond fp32 rounding.  The kernel is persistent and gives every warp one
+ *   contiguous range of (sequence, KV head, page) work.
  * Replaces triton_decode._decode_parts (triton_decode.py:35-67). */
 int akv_decode_partials(const void *arena, int64_t arena_bytes, const int64_t *table,
                         int64_t table_stride, const int32_t *seq_blocks, int32_t max_blocks,
