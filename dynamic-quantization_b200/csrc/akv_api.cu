@@ -14,7 +14,8 @@ extern "C" const char *akv_status_string(int status) {
   }
 }
 
-extern "C" int akv_abi_version(void) { return 2; }
+// 3: V payloads stored in the bank-swizzled byte order (records of version 2 read differently).
+extern "C" int akv_abi_version(void) { return 3; }
 
 extern "C" int64_t akv_record_bytes(int head_dim, int group, int mode) {
   if (head_dim <= 0 || group <= 0 || (16 * head_dim) % group) return -1;

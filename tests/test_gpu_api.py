@@ -203,6 +203,36 @@ def test_append_demotion_protection_and_partial_page(cuda):
         layer.demote(1, 16)
 
 
+@pytest.mark.parametrize("dim", [64, 128])
+@pytest.mark.parametrize("bits", [4, 8, 16])
+def test_pooled_page_views_hold_pack_page_payloads(cuda, dim, bits):
+    """PagedLayer's page views over the pool (K row-major, V stored in the
+    decode's bank-swizzled byte order behind a byte map) present the payload,
+    scales and values pack_page gives the same 16 tokens (packed_decode.py:48-67);
+    appended rows, a partial page included, read back as written."""
+    torch.manual_seed(dim + bits)
+    tokens = 45
+    layer = akv.PagedLayer(2, dim, 64, archive_bits=bits, recent_pages=0, device=cuda)
+    k = torch.randn(1, 2, tokens, dim).half().to(cuda)
+    v = torch.randn_like(k)
+    for start in range(0, tokens, 9):
+        layer.append(k[:, :, start:start + 9], v[:, :, start:start + 9])
+    assert [pair[0].bits for pair in layer.pages] == [bits, bits, 16]
+    for p, (kp, vp) in enumerate(layer.pages):
+        n = min(16, tokens - 16 * p)
+        for page, src in ((kp, k), (vp, v)):
+            slab = src[0, :, 16 * p:16 * p + n]
+            if page.bits == 16:
+                assert torch.equal(page.data[:, :n], slab)
+                assert not page.data[:, n:].any()
+                continue
+            want = akv.pack_page(slab, page.bits, 64)
+            assert torch.equal(page.data.view(torch.uint8), want.data.view(torch.uint8))
+            assert torch.equal(page.scales, want.scales)
+            assert torch.equal(page.dense(), want.dense())
+    assert akv.take_device_status(cuda) == 0
+
+
 def test_fp16_attention_matches_original_tensors_with_gqa(cuda):
     torch.manual_seed(2)
     key = torch.randn(1, 2, 37, 64).half().to(cuda)
