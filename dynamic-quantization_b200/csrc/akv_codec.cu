@@ -82,26 +82,40 @@ struct Slab {
   static constexpr int kElems = kBlock * D;
 };
 
+// Byte XOR that turns the row-major offset of a lane's 8 elements of chunk c
+// (elements 256c + 8 lane of a [16][D] slab) into their stored offset in a V
+// payload: v_swizzle with the key worked out for these offsets (it depends on
+// c alone for head_dim 128, on c and the lane for head_dim 64).
+template <int D>
+__device__ __forceinline__ int v_chunk_xor(int mode, int c, int lane) {
+  int key;
+  if constexpr (D == 128)
+    key = mode == AKV_MODE_FP16 ? ((c & 1) | ((c & 2) << 1)) : ((2 * c) & 6);
+  else
+    key = mode == AKV_MODE_INT4 ? ((2 * c) & 2) : (((4 * c) & 4) | ((lane >> 3) & 2));
+  return key << 4;
+}
+
 // Dequantize 8 consecutive elements of a record payload to fp16, exactly as
 // QuantizedPage.dense (packed_decode.py:34-45): fp16(int * float(scale)).
 // `vpay`: a V payload, stored in the swizzled byte order (v_swizzle).
-template <int D, int G>
+template <int D, int G, bool VPAY>
 __device__ __forceinline__ uint4 record_load8(int mode, const uint8_t *payload, const __half *sc,
-                                              int c, int lane, bool vpay) {
+                                              int c, int lane) {
   const int e = 256 * c + 8 * lane;
-  auto at = [&](int64_t o) { return payload + (vpay ? v_swizzle(D, mode, o) : o); };
-  if (mode == AKV_MODE_FP16) return *reinterpret_cast<const uint4 *>(at(2 * e));
+  const int vx = VPAY ? v_chunk_xor<D>(mode, c, lane) : 0;
+  if (mode == AKV_MODE_FP16) return *reinterpret_cast<const uint4 *>(payload + ((2 * e) ^ vx));
   const float s = __half2float(sc[e / G]);
   int q[8];
   if (mode == AKV_MODE_INT8) {
-    const uint2 w = *reinterpret_cast<const uint2 *>(at(e));
+    const uint2 w = *reinterpret_cast<const uint2 *>(payload + (e ^ vx));
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       q[i] = (int)(int8_t)(w.x >> (8 * i));
       q[4 + i] = (int)(int8_t)(w.y >> (8 * i));
     }
   } else {
-    const uint32_t w = *reinterpret_cast<const uint32_t *>(at(e / 2));
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(payload + ((e / 2) ^ vx));
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       int n = (w >> (4 * i)) & 15;
@@ -201,10 +215,12 @@ template <int D, int G, int SEM>
 __device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], int mode,
                                            uint8_t *payload, __half *sc, int lane, bool vpay) {
   constexpr int NC = Slab<D>::kChunks;
-  auto at = [&](int64_t o) { return payload + (vpay ? v_swizzle(D, mode, o) : o); };
   if (mode == AKV_MODE_FP16) {
 #pragma unroll
-    for (int c = 0; c < NC; ++c) *reinterpret_cast<uint4 *>(at(512 * c + 16 * lane)) = v[c];
+    for (int c = 0; c < NC; ++c) {
+      const int vx = vpay ? v_chunk_xor<D>(mode, c, lane) : 0;
+      *reinterpret_cast<uint4 *>(payload + ((512 * c + 16 * lane) ^ vx)) = v[c];
+    }
     return;
   }
   const float qmax = mode == AKV_MODE_INT8 ? 127.f : 7.f;
@@ -246,15 +262,16 @@ __device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], i
     uint32_t t[8];
     quantize_chunk(v[c], gs.divisor, r, qmax, t);
     const int e = 256 * c + 8 * lane;
+    const int vx = vpay ? v_chunk_xor<D>(mode, c, lane) : 0;
     if (mode == AKV_MODE_INT8) {
       const uint32_t w0 = prmt(prmt(t[0], t[1], 0x0040u), prmt(t[2], t[3], 0x0040u), 0x5410u);
       const uint32_t w1 = prmt(prmt(t[4], t[5], 0x0040u), prmt(t[6], t[7], 0x0040u), 0x5410u);
-      *reinterpret_cast<uint2 *>(at(e)) = make_uint2(w0, w1);
+      *reinterpret_cast<uint2 *>(payload + (e ^ vx)) = make_uint2(w0, w1);
     } else {
       uint32_t pb[4];  // byte k: element 2k in the low nibble, 2k+1 in the high nibble
 #pragma unroll
       for (int k = 0; k < 4; ++k) pb[k] = (t[2 * k] & 0x0fu) | ((t[2 * k + 1] << 4) & 0xf0u);
-      *reinterpret_cast<uint32_t *>(at(e / 2)) =
+      *reinterpret_cast<uint32_t *>(payload + ((e / 2) ^ vx)) =
           prmt(prmt(pb[0], pb[1], 0x0040u), prmt(pb[2], pb[3], 0x0040u), 0x5410u);
     }
     if (e % G == 0) sc[e / G] = gs.stored;
@@ -268,9 +285,11 @@ __device__ __forceinline__ bool page_in_arena(int64_t desc, int64_t page_bytes, 
 }
 
 // Pack (SRC_RECORD = false: dense fp16 source) or repack (SRC_RECORD = true:
-// source records in the arena) one slab per warp.
+// source records in the arena) one slab per warp.  A repack holds both the
+// source record's reads and the destination's stores, so it runs 2 CTAs per
+// SM (up to 128 registers) rather than 3 (85), where it would spill.
 template <int D, int G, int SEM, bool SRC_RECORD>
-__global__ void __launch_bounds__(256, 3) pack_pages_kernel(
+__global__ void __launch_bounds__(256, SRC_RECORD ? 2 : 3) pack_pages_kernel(
     const __half *__restrict__ src_k, const __half *__restrict__ src_v, int64_t outer_stride,
     int64_t head_stride, int64_t blocks_per_row, const int64_t *__restrict__ src_desc,
     const int64_t *__restrict__ dst_desc, int64_t n_pages, uint8_t *__restrict__ arena,
@@ -306,8 +325,13 @@ __global__ void __launch_bounds__(256, 3) pack_pages_kernel(
       const uint8_t *pay = rec + kv * pb;
       const __half *sc =
           reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, smode);
+      if (kv) {
 #pragma unroll
-      for (int c = 0; c < NC; ++c) v[c] = record_load8<D, G>(smode, pay, sc, c, lane, kv == 1);
+        for (int c = 0; c < NC; ++c) v[c] = record_load8<D, G, true>(smode, pay, sc, c, lane);
+      } else {
+#pragma unroll
+        for (int c = 0; c < NC; ++c) v[c] = record_load8<D, G, false>(smode, pay, sc, c, lane);
+      }
     } else {
       const __half *src = (kv ? src_v : src_k) + (p / blocks_per_row) * outer_stride +
                           h * head_stride + (p % blocks_per_row) * (int64_t)kBlock * D;
@@ -357,7 +381,8 @@ __global__ void __launch_bounds__(256) unpack_pages_kernel(const int64_t *__rest
         const uint8_t *rec = arena + desc_offset(d) + h * rb;
         const int64_t pb = payload_bytes(D, mode);
         const __half *sc = reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, mode);
-        v = record_load8<D, G>(mode, rec + kv * pb, sc, c, lane, kv == 1);
+        v = kv ? record_load8<D, G, true>(mode, rec + pb, sc, c, lane)
+               : record_load8<D, G, false>(mode, rec, sc, c, lane);
       }
       *reinterpret_cast<uint4 *>(out + 256 * c + 8 * lane) = v;
     }
