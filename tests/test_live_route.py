@@ -5,6 +5,9 @@ No checkpoint is available offline, so the models are randomly initialised
 Qwen3 architectures (fp16 on the GPU); the gate compares two attention
 implementations over the same stores, which holds for any weights."""
 
+import gc
+import weakref
+
 import pytest
 import torch
 
@@ -75,6 +78,12 @@ def test_live_cache_appends_and_demotes_during_decode(cuda):
     assert after["tokens"] == before["tokens"] + 40 == 139
     assert after["demotions"] > before["demotions"]
     assert after["payload_bytes"] < 2 * 2 * 2 * 8 * 139 * 128  # below the FP16 size of two layers' K and V
+    # The global attention registry keeps no closure over the cache once the
+    # route has exited (colab_experiment.py:147-148): the cache is freed.
+    cache_ref = weakref.ref(cache)
+    del cache
+    gc.collect()
+    assert cache_ref() is None, "the attention registry retained the live cache"
 
 
 def test_controlled_decode_validates_like_the_reference():
