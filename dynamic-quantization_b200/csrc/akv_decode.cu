@@ -1132,8 +1132,10 @@ static int device_ctas(int *out) {
   return AKV_OK;
 }
 
+// expand: cut finer than `splits` asks while the device has warps to spare
+// (false: exactly min(resident warps, items * splits) pieces).
 static int make_plan(int batch, int q_heads, int kv_heads, int head_dim, int max_blocks, int splits,
-                     Plan *plan) {
+                     Plan *plan, bool expand = true) {
   if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || max_blocks < 0 || q_heads % kv_heads)
     return AKV_ERR_INVALID;
   if (head_dim != 64 && head_dim != 128) return AKV_ERR_UNSUPPORTED;
@@ -1155,7 +1157,8 @@ static int make_plan(int batch, int q_heads, int kv_heads, int head_dim, int max
   // kMinPagesPerWarp entries a warp) while the device has warps to spare.
   if (splits > 0)
     warps = std::min<int64_t>(warps, std::max<int64_t>(items * (int64_t)splits,
-                                                       (total + kMinPagesPerWarp - 1) / kMinPagesPerWarp));
+                                                       expand ? (total + kMinPagesPerWarp - 1) / kMinPagesPerWarp
+                                                              : 0));
   warps = std::max<int64_t>(1, std::min<int64_t>(warps, std::max<int64_t>(total, 1)));
   const int64_t range = std::max<int64_t>(1, (total + warps - 1) / warps);
   warps = std::max<int64_t>(1, (total + range - 1) / range);
@@ -1222,6 +1225,11 @@ static int decode_launch(const void *arena, int64_t arena_bytes, const int64_t *
   if (lg < 0 || group < head_dim / 4 || group > 16 * head_dim) return AKV_ERR_UNSUPPORTED;
   Plan pl;
   if (int st = make_plan(batch, q_heads, kv_heads, head_dim, max_blocks, splits, &pl)) return st;
+  // A workspace sized for exactly `splits` pieces per item (akv_workspace_bytes
+  // sizes it for the finer cut) still runs, with that decomposition.
+  if (workspace_bytes < pl.bytes &&
+      make_plan(batch, q_heads, kv_heads, head_dim, max_blocks, splits, &pl, false) != AKV_OK)
+    return AKV_ERR_INVALID;
   if (workspace_bytes < pl.bytes) return AKV_ERR_INVALID;
   DecodeParams p;
   p.arena = (const uint8_t *)arena;
@@ -1430,9 +1438,15 @@ extern "C" int akv_packed_attention_static(const void *arena, int64_t arena_byte
                                            int32_t splits, void *out, int64_t out_batch_stride,
                                            int64_t out_head_stride, int32_t *dev_status, void *stream) {
   if (!out) return AKV_ERR_INVALID;
-  const int64_t need = akv_workspace_bytes(batch, q_heads, kv_heads, head_dim, max_blocks, splits);
+  int64_t need = akv_workspace_bytes(batch, q_heads, kv_heads, head_dim, max_blocks, splits);
   if (need <= 0) return AKV_ERR_INVALID;
-  if (need > akv::kStaticScratchBytes) return AKV_ERR_SCRATCH;
+  if (need > akv::kStaticScratchBytes) {  // try exactly `splits` pieces per item, without the finer cut
+    akv::Plan pl;
+    if (akv::make_plan(batch, q_heads, kv_heads, head_dim, max_blocks, splits, &pl, false) != AKV_OK)
+      return AKV_ERR_INVALID;
+    if (pl.bytes > akv::kStaticScratchBytes) return AKV_ERR_SCRATCH;
+    need = akv::kStaticScratchBytes;  // the decode picks the decomposition that fits
+  }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return AKV_ERR_CUDA;
   void *scratch = nullptr;

@@ -124,7 +124,10 @@ int akv_unpack_pages(const int64_t *desc, int64_t n_pages, const void *arena,
  * The workspace holds a 256-byte header describing the work decomposition and
  * one partial state (acc[head_dim], m, l) per (warp, item it touched, query
  * head); it is opaque to the caller and needs no initialisation.  Calls that
- * use one workspace must be ordered (one stream, or events between streams). */
+ * use one workspace must be ordered (one stream, or events between streams).
+ * The size is for the decode's finer cut of the work (see `splits` below); a
+ * workspace that only holds exactly `splits` pieces per (sequence, KV head)
+ * also works, with that decomposition. */
 int64_t akv_workspace_bytes(int batch, int q_heads, int kv_heads, int head_dim, int max_blocks,
                             int splits);
 
@@ -218,8 +221,9 @@ int akv_packed_attention(const void *arena, int64_t arena_bytes, const int64_t *
  * would synchronize the device, bindings holding raw pointers but no allocator.
  * The split-K partials live in a fixed array inside the library
  * (akv_static_scratch_bytes() = 8 MiB per GPU, held until process exit), so it
- * allocates nothing; requests whose akv_workspace_bytes exceed that return
- * AKV_ERR_SCRATCH.
+ * allocates nothing.  When the finer cut of the work (see `splits`) needs more,
+ * the call runs with exactly `splits` pieces per (sequence, KV head) instead;
+ * requests whose partial states exceed 8 MiB even then return AKV_ERR_SCRATCH.
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before
  * any stream capture.  All calls on a device share the array and it keeps the

@@ -93,3 +93,16 @@ def test_static_scratch_refuses_requests_beyond_its_size(cuda):
                                              _lib.stream_of(cuda))
     assert status == _lib.ERR_SCRATCH
     assert "8 MiB" in _lib.status_string(status)
+
+
+def test_static_scratch_runs_a_long_sequence_with_the_requested_splits(cuda):
+    """A single long sequence whose finer cut of the work (every resident warp)
+    would need more than the fixed scratch runs with exactly `splits` pieces
+    per (sequence, KV head) instead, and matches the workspace entry."""
+    lib = _lib.load()
+    q, store = _store(cuda, 801, batch=1, q_heads=64, kv_heads=8, tokens=32768, group=2048)
+    splits = 4
+    assert lib.akv_workspace_bytes(1, 64, 8, 128, store.max_blocks, splits) > lib.akv_static_scratch_bytes()
+    got = _static(q, store, splits, cuda)
+    want = _with_workspace(q, store, splits, cuda)
+    np.testing.assert_allclose(got.float().cpu().numpy(), want.float().cpu().numpy(), atol=ATOL, rtol=RTOL)
