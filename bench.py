@@ -852,6 +852,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference", "reference_gpu"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["long", "pack", "pack_small"], default="batched")
+    ap.add_argument("--mix", choices=("fp16", "int8", "int4"), default=None,
+                    help="profiling: every page of a batched workload in this one precision")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -880,6 +882,9 @@ def main():
             run_long(args, LONG)
         return
     wl = WORKLOADS[args.workload]
+    if args.mix:
+        bits = {"fp16": 16, "int8": 8, "int4": 4}[args.mix]
+        wl = dict(wl, name=f"{wl['name']}, all pages {args.mix}", mix={b: float(b == bits) for b in (16, 8, 4, 0)})
     if args.impl == "reference":
         run_reference(args, wl)
     else:
