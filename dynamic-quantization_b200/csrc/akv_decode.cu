@@ -16,7 +16,10 @@
 //    invisible pages without reading them, and bulk-copies each record
 //    (cp.async.bulk, mbarrier completion, no multicast; lane 0 issues) into a
 //    private 13 KB shared-memory ring the moment it frees room, so the copy
-//    pipeline needs no hand-off between warps;
+//    pipeline needs no hand-off between warps; an SM's 16 warps form one CTA,
+//    so they share one scheduler age and finish together;
+//  * V payloads are stored with their 16-byte units swizzled inside 128-byte
+//    lines (v_swizzle), so the V fragment loads from the ring hit 32 banks;
 //  * INT8 and INT4 pages travel in pairs (two pages of one item and mode, one
 //    ring slot, one barrier, one softmax step), which halves the per-page
 //    control work of the loop;
