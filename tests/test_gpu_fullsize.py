@@ -6,7 +6,10 @@ Two size-independent checks:
   the oracle on small cases), skipped pages masked out, agrees with ``packed_attention`` within the
   decode's tolerance against the reference (max-abs 2e-3, rel 1e-2);
 * the log-sum-exp merge identity (triton_decode.py:70-82 algebra): the decode of a store equals the
-  merge of the decodes of its two page halves, within fp32 rounding.
+  merge of the decodes of its two page halves, within fp32 rounding;
+* the pack kernel over one layer of the pack workload gives, bit for bit, the values of a torch
+  restatement of quantize_tensor + dequantize (the reference's own function, run on CPU over sampled
+  blocks, agrees with both).
 
 Geometries: one layer of the batched workload (64 sequences x 8192 tokens, 16 query / 8 KV heads,
 head_dim 128, pages 15/35/40/10 % FP16/INT8/INT4/evicted) and one 1,048,576-token sequence (32 query
@@ -108,3 +111,42 @@ def test_full_size_long_sequence_equals_merge_of_its_halves(cuda):
     merged = akv.merge_states(torch.stack(states))
     assert akv.take_device_status(cuda) == 0
     torch.testing.assert_close(merged.float(), full.float(), atol=1e-3, rtol=1e-3)
+
+
+def _quantized_values(x, bits):
+    """What the reference attends over for blocks ``[n, 2048]`` (one per page and KV head):
+    quantize_tensor (backend.py:210-219: fp32 absmax / qmax, 1 for an all-zero group, round half to
+    even of x / scale, clamp, int8, fp16 scale after the division) then fp16(int * float(scale))."""
+    xf = x.float()
+    qmax = 127.0 if bits == 8 else 7.0
+    amax = xf.abs().amax(dim=1, keepdim=True)
+    # A tensor divisor: torch on CUDA turns division by a Python scalar into a multiply by its
+    # reciprocal, which is not the correctly rounded quotient of the reference's division.
+    scale = torch.where(amax == 0, torch.ones_like(amax), amax / torch.full_like(amax, qmax))
+    # Through int8 as in the reference: a value that rounds to zero dequantises to +0, never -0.
+    q = torch.round(xf / scale).clamp(-qmax, qmax).to(torch.int8).float()
+    return (q * scale.half().float()).half()
+
+
+def test_full_size_pack_matches_quantize_tensor_bit_for_bit(cuda):
+    """One layer of the pack workload (32 sequences x 8 KV heads x 4096 tokens, 20/30/50 %
+    FP16/INT8/INT4 pages, one scale per (page, KV head)): the values read back from the records are
+    those of quantize_tensor then dequantize, bit for bit."""
+    batch, heads, tokens = 32, 8, 4096
+    gen = torch.Generator(device=cuda).manual_seed(11)
+    k = _kv(gen, (batch, heads, tokens, D), cuda)
+    v = _kv(gen, (batch, heads, tokens, D), cuda)
+    bits = np.random.default_rng(11).choice(np.array([16, 8, 4]), size=(batch, tokens // 16), p=[.2, .3, .5])
+    pool = P.PagePool(heads, D, group=16 * D, pages={b: int((bits == b).sum()) for b in (16, 8, 4)}, device=cuda)
+    store = P.pack_dense(pool, k, v, bits, semantics="tensor")
+    dk, dv, _ = _dense(store, 0, batch)
+    assert akv.take_device_status(cuda) == 0
+    mode = torch.from_numpy(bits).to(cuda)[:, None, :].expand(batch, heads, -1).reshape(-1)
+    for name, src, got in (("K", k, dk), ("V", v, dv)):
+        blocks = src.reshape(batch, heads, tokens // 16, 16 * D).reshape(-1, 16 * D)
+        read = got.reshape(batch, heads, tokens // 16, 16 * D).reshape(-1, 16 * D)
+        for b in (16, 8, 4):
+            sel = mode == b
+            want = blocks[sel] if b == 16 else _quantized_values(blocks[sel], b)
+            bad = int((read[sel].view(torch.int16) != want.view(torch.int16)).sum())
+            assert bad == 0, f"{name}: {bad} values of the {b}-bit pages differ"
