@@ -135,6 +135,7 @@ __device__ __forceinline__ void lds_words(const uint8_t *p, uint32_t (&w)[N]) {
 // 2t4+8, 2t4+9 at column gid*DV.  Two 16-bit indices per word.
 struct ScaleIdx {
   uint32_t k, vab, vcd;
+  uint32_t vo;  // the lane's stored V row-2t4 offset: INT4 bits 0-9, INT8 10-19, FP16 20-31
   __device__ __forceinline__ int k0() const { return (int)(k & 0xffff); }
   __device__ __forceinline__ int k1() const { return (int)(k >> 16); }
   __device__ __forceinline__ int va() const { return (int)(vab & 0xffff); }
@@ -234,11 +235,13 @@ __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, 
   constexpr int WP = W / PARTS;
   constexpr int TP = (D / 16) / PARTS;        // m-tiles per part
   // Stored offsets of the lane's row slices in the swizzled V payload
-  // (v_swizzle): row 2t4 is c0; the second half of a 32-byte slice flips bit
+  // (v_swizzle): row 2t4 is c0 (worked out once per kernel into si.vo for the
+  // three modes); the second half of a 32-byte slice flips bit
   // 4; row 2t4+1 flips the row bit of a line holding two or four rows, or is
   // one row further; rows +8 are 8 rows further.  Within each phase of the
   // shared-memory load the lanes hit distinct banks.
-  const int c0 = (int)v_swizzle(D, MODE, (2 * t4) * rowB + gid * (W * 4));
+  const int c0 = (int)((si.vo >> (MODE == AKV_MODE_INT4 ? 0 : (MODE == AKV_MODE_INT8 ? 10 : 20))) &
+                        (MODE == AKV_MODE_FP16 ? 0xfffu : 0x3ffu));
   constexpr int kOddRow = rowB == 64 ? 64 : (rowB == 32 ? 32 : 0);
   auto sc = [](uint32_t x, uint32_t s) { return FOLD ? x : hmul2(x, s); };
   uint32_t sab = 0, scd = 0;
@@ -365,7 +368,7 @@ __device__ __forceinline__ void zero_tail(uint8_t *rec, int ntok, int lane) {
 
 // One FP16 page.
 template <int D, bool SLAB>
-__device__ __forceinline__ void fp16_attend(uint8_t *rec, int ntok, int lane,
+__device__ __forceinline__ void fp16_attend(uint8_t *rec, int ntok, int lane, const ScaleIdx &si,
                                             const uint32_t (&qf)[D / 16][2], float scale_log2,
                                             SoftmaxState &st, float (&o)[D / 16][4]) {
   constexpr int PB = kBlock * D * 2;
@@ -374,14 +377,14 @@ __device__ __forceinline__ void fp16_attend(uint8_t *rec, int ntok, int lane,
     zero_tail<D, AKV_MODE_FP16>(rec, ntok, lane);
     __syncwarp();
   }
-  const ScaleIdx none{0, 0, 0};
+  const ScaleIdx none{0, 0, 0, 0};
   float s[1][4];
   uint32_t b[1][2];
   const int nt[1] = {ntok};
   const float ps[1] = {1.f};
   page_qk<D, AKV_MODE_FP16, SLAB>(rec, nullptr, none, gid, t4, qf, s[0]);
   pages_softmax<D, 1>(s, nt, false, gid, scale_log2, 8.f, ps, st, o, b);
-  page_pv<D, AKV_MODE_FP16, SLAB, false>(rec + PB, nullptr, none, gid, t4, b[0][0], b[0][1], o);
+  page_pv<D, AKV_MODE_FP16, SLAB, false>(rec + PB, nullptr, si, gid, t4, b[0][0], b[0][1], o);
 }
 
 // A slot of one or two INT8/INT4 pages of one item, adjacent in the ring
@@ -517,6 +520,9 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kMaxThreads, 1)
            ((uint32_t)(((2 * t4 + 1) * D + gid * T::DV) >> lg) << 16);
   si.vcd = (uint32_t)(((2 * t4 + 8) * D + gid * T::DV) >> lg) |
            ((uint32_t)(((2 * t4 + 9) * D + gid * T::DV) >> lg) << 16);
+  si.vo = (uint32_t)v_swizzle(D, AKV_MODE_INT4, (2 * t4) * (D / 2) + gid * (T::DV / 2)) |
+          ((uint32_t)v_swizzle(D, AKV_MODE_INT8, (2 * t4) * D + gid * T::DV) << 10) |
+          ((uint32_t)v_swizzle(D, AKV_MODE_FP16, (2 * t4) * (2 * D) + gid * (2 * T::DV)) << 20);
   const uint32_t scale_bytes = 2u * (uint32_t)((kBlock * D) >> lg);
   const uint32_t rb4 = (2u * (uint32_t)payload_bytes(D, AKV_MODE_INT4) + 2u * scale_bytes + 15u) & ~15u;
   const uint32_t rb8 = (2u * (uint32_t)payload_bytes(D, AKV_MODE_INT8) + 2u * scale_bytes + 15u) & ~15u;
@@ -732,7 +738,7 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kMaxThreads, 1)
         slot_attend<D, AKV_MODE_INT8, SLAB>(rec, rb8, has2, ntok, ntok1, lane, lg, si, qf, p.scale_log2, st, o);
         break;
       default:
-        fp16_attend<D, SLAB>(rec, ntok, lane, qf, p.scale_log2, st, o);
+        fp16_attend<D, SLAB>(rec, ntok, lane, si, qf, p.scale_log2, st, o);
         break;
     }
     __syncwarp();
