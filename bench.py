@@ -847,15 +847,19 @@ def run_reference_gpu(args):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
-    ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", choices=("ours", "reference", "reference_gpu"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["long", "pack", "pack_small"], default="batched")
+    ap.add_argument("--gpus", type=int, default=1, help="GPUs of one node, one process each (torchrun for N > 1)")
+    ap.add_argument("--steps", type=int, default=300, help="timed steps (one decode token per sequence, all layers)")
+    ap.add_argument("--warmup", type=int, default=10, help="untimed steps first (at least 3)")
+    ap.add_argument("--impl", choices=("ours", "reference", "reference_gpu"), default="ours",
+                    help="ours: the CUDA kernels; reference: the reference's CPU decode path (timed on the "
+                         "host cores); reference_gpu: the reference's own Triton decode beside ours, batch 1")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["long", "pack", "pack_small"], default="batched",
+                    help="batched (default), large, long (one 1M-token sequence), pack (requantize); "
+                         "*_small: one-layer profiling cases")
     ap.add_argument("--mix", choices=("fp16", "int8", "int4"), default=None,
                     help="profiling: every page of a batched workload in this one precision")
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="seconds of CPU timing for the CPU baseline")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
