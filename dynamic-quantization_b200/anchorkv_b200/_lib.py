@@ -76,6 +76,9 @@ _lib = None
 def load(path: Path | str = LIB_PATH) -> ctypes.CDLL:
     """Load (once) and return the library with its prototypes set."""
     global _lib
+    lib = _lib
+    if lib is not None:  # loaded: no lock on the per-call path
+        return lib
     with _lock:
         if _lib is None:
             p = Path(path)

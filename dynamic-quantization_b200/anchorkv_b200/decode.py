@@ -22,10 +22,23 @@ from . import _lib
 from .pool import PagedBatch, group_ok
 
 _workspaces: dict = {}
+_workspace_sizes: dict = {}
 
 
-def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+def _workspace_bytes(device: torch.device, *geometry) -> int:
+    """akv_workspace_bytes for ``geometry`` on ``device``, remembered (it depends only on them)."""
+    key = (device.index, geometry)
+    nbytes = _workspace_sizes.get(key)
+    if nbytes is None:
+        if len(_workspace_sizes) > 4096:
+            _workspace_sizes.clear()
+        nbytes = _lib.load().akv_workspace_bytes(*geometry)
+        _workspace_sizes[key] = nbytes
+    return nbytes
+
+
+def _workspace(device: torch.device, nbytes: int, stream: int | None = None) -> torch.Tensor:
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream if stream is None else stream)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
@@ -72,15 +85,16 @@ def packed_attention(query, layer, scale, splits=4, *, out=None):
     if out is None:
         out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
     dev = query.device
-    nbytes = _lib.load().akv_workspace_bytes(batch, heads, layer.heads, layer.dim, max_blocks, splits)
+    nbytes = _workspace_bytes(dev, batch, heads, layer.heads, layer.dim, max_blocks, splits)
     if nbytes < 0:
         raise ValueError('unsupported decode geometry')
-    ws = _workspace(dev, nbytes)
+    stream = _lib.stream_of(dev)
+    ws = _workspace(dev, nbytes, stream)
     _lib.call("akv_packed_attention", arena.data_ptr(), arena_bytes, table.data_ptr(), table.stride(0),
               None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks,
               query.data_ptr(), query.stride(0), query.stride(1), batch, heads, layer.heads, layer.dim,
               layer.group, float(scale), splits, out.data_ptr(), out.stride(0), out.stride(1),
-              ws.data_ptr(), ws.numel(), _lib.status_word(dev).data_ptr(), _lib.stream_of(dev))
+              ws.data_ptr(), ws.numel(), _lib.status_word(dev).data_ptr(), stream)
     return out
 
 
