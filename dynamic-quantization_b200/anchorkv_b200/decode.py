@@ -110,12 +110,12 @@ def decode_partial_states(query, layer, scale, splits=0):
     query = query.contiguous()
     arena, arena_bytes, table, seq_blocks, max_blocks = _store_geometry(layer)
     dev = query.device
-    nbytes = _lib.load().akv_workspace_bytes(batch, heads, layer.heads, layer.dim, max_blocks, splits)
+    nbytes = _workspace_bytes(dev, batch, heads, layer.heads, layer.dim, max_blocks, splits)
     if nbytes < 0:
         raise ValueError('unsupported decode geometry')
-    ws = _workspace(dev, nbytes)
-    state = torch.empty((batch, heads, layer.dim + 2), dtype=torch.float32, device=dev)
     stream = _lib.stream_of(dev)
+    ws = _workspace(dev, nbytes, stream)
+    state = torch.empty((batch, heads, layer.dim + 2), dtype=torch.float32, device=dev)
     status = _lib.status_word(dev).data_ptr()
     _lib.call("akv_decode_partials", arena.data_ptr(), arena_bytes, table.data_ptr(), table.stride(0),
               None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks, query.data_ptr(),
