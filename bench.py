@@ -95,16 +95,16 @@ def hbm_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def traffic_from_profile(name: str):
-    """DRAM bytes per launch from the committed ncu summary ``profiles/<name>.md``
-    (its ``traffic_bytes_per_launch:`` line), if present."""
-    f = ROOT / "profiles" / f"{name}.md"
+def traffic_for(name: str):
+    """DRAM traffic per launch of kernel case ``name`` from ``profiles/traffic.json``
+    (one ncu capture each, with the command that made it), or None."""
+    f = ROOT / "profiles" / "traffic.json"
     if not f.exists():
         return None
-    for line in f.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            return float(line.split(":", 1)[1])
-    return None
+    entry = json.loads(f.read_text()).get(name)
+    if not entry:
+        return None
+    return {"bytes_per_launch": float(entry["bytes_per_launch"]), "source": entry["source"]}
 
 
 class ClockSampler:
@@ -146,12 +146,40 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- CPU baseline
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def import_reference():
+    """The unmodified reference package installed in baseline/_ref: returns
+    (packed_decode module, None) or (None, why it is not importable)."""
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    try:
+        from anchorkv import packed_decode as ref_pd
+    except Exception as exc:  # not installed here, or a dependency is missing
+        return None, f"reference not importable from {REF_DIR}: {type(exc).__name__}: {exc}"
+    return ref_pd, None
+
+
 def cpu_baseline(wl: dict, seed: int, seconds: float, calls_min: int = 3):
-    """Time the reference's CPU decode path (restated with torch CPU ops) on one
-    sequence-layer of the workload for about ``seconds``; returns a dict."""
+    """Time the reference's own CPU decode path on one sequence-layer of the
+    workload for about ``seconds`` with all host cores; returns a dict.
+
+    The reference (baseline/_ref, unmodified) holds a batch-one sequence in its
+    ``PagedLayer`` (packed_decode.py:108-194) and decodes with
+    ``dense_attention`` (packed_decode.py:197-203): every call dequantises all
+    pages to fp16, concatenates them and runs SDPA.  Its layer has no eviction,
+    so evicted blocks are left out of it, as ``materialize_segments`` drops them
+    (backend.py:557-591); each kept page is demoted to the block's precision with
+    ``PagedLayer.demote``.  Its pages take one scale per 64 elements (the layer
+    requires groups along head_dim), the workload's one per (block, KV head):
+    bytes are counted in the workload's layout, as for the GPU arm.  If the
+    reference cannot be imported, the CPU restatement in oracle/baseline.py is
+    timed instead and the result says so."""
+    import numpy as np
     import torch
 
-    from oracle import baseline as OB
+    from anchorkv_b200 import pool as P
 
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
@@ -159,29 +187,60 @@ def cpu_baseline(wl: dict, seed: int, seconds: float, calls_min: int = 3):
     # tokens/s is scaled by the number of slices.
     blocks = min(wl["tokens"], 65536) // 16
     slices = wl["tokens"] // (blocks * 16)
-    bits = OB.random_bits(seed, blocks, wl["mix"])
-    pages = OB.build_sequence(seed, wl["kv_heads"], wl["dim"], blocks, bits, wl["group"])
-    q = torch.randn(1, wl["q_heads"], 1, wl["dim"], generator=torch.Generator().manual_seed(seed)).half()
-    scale = 1 / math.sqrt(wl["dim"])
-    OB.decode_cpu(pages, q, scale)  # warm
+    Hq, Hkv, D = wl["q_heads"], wl["kv_heads"], wl["dim"]
+    keys = list(wl["mix"])
+    bits = np.random.default_rng(seed).choice(np.array(keys), size=blocks, p=[wl["mix"][k] for k in keys])
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, Hq, 1, D, generator=gen).half()
+    scale = 1 / math.sqrt(D)
+    nbytes = sum(P.algorithmic_record_bytes(D, wl["group"], int(b)) * Hkv for b in bits if b) + 2 * q.numel() * 2
+    ref_pd, why = import_reference()
+    if ref_pd is not None:
+        kept = np.nonzero(bits)[0]
+        k = torch.randn(1, Hkv, blocks * 16, D, generator=gen).half()
+        v = torch.randn(1, Hkv, blocks * 16, D, generator=gen).half()
+        tok = torch.from_numpy((kept[:, None] * 16 + np.arange(16)[None, :]).reshape(-1))
+        layer = ref_pd.PagedLayer(Hkv, D, len(tok), group=64, archive_bits=16, device="cpu")
+        layer.append(k[:, :, tok], v[:, :, tok])
+        for page, b in enumerate(bits[kept]):
+            if b != 16:
+                layer.demote(page, int(b))
+
+        def call():
+            return ref_pd.dense_attention(q, layer, scale)
+
+        kind, what = "reference", ("the reference's PagedLayer (baseline/_ref, unmodified; group 64) + "
+                                   "dense_attention")
+    else:
+        from oracle import baseline as OB
+
+        pages = OB.build_sequence(seed, Hkv, D, blocks, bits, wl["group"])
+
+        def call():
+            return OB.decode_cpu(pages, q, scale)
+
+        kind, what = "port", f"fallback, {why}: the CPU restatement oracle/baseline.decode_cpu"
+    call()  # warm
     times = []
     t_end = time.perf_counter() + seconds
     while len(times) < calls_min or time.perf_counter() < t_end:
         t0 = time.perf_counter()
-        OB.decode_cpu(pages, q, scale)
+        call()
         times.append(time.perf_counter() - t0)
     per_call = statistics.median(times)
-    nbytes = OB.resident_bytes(pages) + 2 * q.numel() * 2
     calls_per_step = wl["layers"] * wl["batch"] * slices
     return {
         "gbs": nbytes / per_call / 1e9,
         "tokens_per_s": wl["batch"] / (per_call * calls_per_step),
         "cores": cores,
+        "kind": kind,
         "calls": len(times),
         "seconds_per_call": per_call,
-        "sample": (f"{len(times)} decode calls of one sequence-layer slice ({blocks} pages, "
-                   f"{wl['kv_heads']} KV heads, same precision mix), median per call; "
-                   f"tokens/s extrapolated x{calls_per_step} calls per step"),
+        "seconds_timed": sum(times),
+        "calls_per_step": calls_per_step,
+        "sample": (f"{len(times)} decode calls of {what} on one sequence-layer slice ({blocks} pages, "
+                   f"{Hkv} KV heads, the workload's precision mix), median per call, {cores} threads; "
+                   f"a full step is {calls_per_step} such calls"),
     }
 
 
@@ -201,6 +260,46 @@ def layer_store_bytes(wl: dict, batch: int) -> float:
     return pages * per_page
 
 
+def workload_bits(wl: dict, seed: int, batch: int, distinct: int):
+    """Per-page precisions (16 / 8 / 4 / 0 = evicted) of ``distinct`` layer stores."""
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    keys = list(wl["mix"])
+    probs = np.array([wl["mix"][k] for k in keys])
+    return [rng.choice(np.array(keys), size=(batch, wl["tokens"] // 16), p=probs) for _ in range(distinct)]
+
+
+def batched_plan(wl: dict, world: int):
+    """(sequences per rank, distinct layer stores per rank, arena bytes of rank 0's pool):
+    what run_ours builds, worked out on the host."""
+    from anchorkv_b200 import pool as P
+
+    strong = bool(wl.get("strong"))
+    B = wl["batch"] // world if strong else wl["batch"]
+    distinct = max(1, min(wl["layers"], int(STORE_BUDGET // layer_store_bytes(wl, B))))
+    bits = workload_bits(wl, 1234, B, distinct)
+    arena = sum(int(sum((x == b).sum() for x in bits)) * wl["kv_heads"] * P.record_bytes(wl["dim"], wl["group"], b)
+                for b in (16, 8, 4))
+    return B, distinct, max(arena, 16)
+
+
+def batched_config(wl: dict, world: int, B: int, distinct: int, arena_bytes: int) -> dict:
+    """The ``config`` of a batched/large line (both arms print the same one)."""
+    strong = bool(wl.get("strong"))
+    return {
+        "workload": wl["name"], "layers": wl["layers"], "q_heads": wl["q_heads"], "kv_heads": wl["kv_heads"],
+        "head_dim": wl["dim"], "batch_per_gpu": B, "context_tokens": wl["tokens"], "page_tokens": 16,
+        "precision_mix": {"fp16": wl["mix"][16], "int8": wl["mix"][8], "int4": wl["mix"][4],
+                          "evicted": wl["mix"][0]},
+        "scale_group": wl["group"], "split_k": wl["splits"],
+        "kv_pool_gb_per_gpu": round(arena_bytes / 1e9, 2),
+        "distinct_layer_stores": distinct,
+        "parallelism": f"batch-sharded x{world} (independent sequences, no collective)",
+        "l2": "inputs larger than L2 (KV pool >> 126 MB), no flush needed",
+    } | ({"strong_scaling_total_batch": wl["batch"]} if strong else {})
+
+
 def build_workload(wl: dict, device, seed: int, batch: int | None = None, distinct: int | None = None):
     """Packed stores for ``distinct`` layers (all of them by default) of ``batch``
     sequences each; layer l of the step uses store l % distinct.  Returns
@@ -212,11 +311,7 @@ def build_workload(wl: dict, device, seed: int, batch: int | None = None, distin
 
     batch = wl["batch"] if batch is None else batch
     distinct = wl["layers"] if distinct is None else distinct
-    rng = np.random.default_rng(seed)
-    nblk = wl["tokens"] // 16
-    keys = list(wl["mix"])
-    probs = np.array([wl["mix"][k] for k in keys])
-    bits = [rng.choice(np.array(keys), size=(batch, nblk), p=probs) for _ in range(distinct)]
+    bits = workload_bits(wl, seed, batch, distinct)
     counts = {b: int(sum((x == b).sum() for x in bits)) for b in (16, 8, 4)}
     pool = P.PagePool(wl["kv_heads"], wl["dim"], group=wl["group"], pages=counts, device=device,
                       shuffle_seed=seed, zero=False)
@@ -263,10 +358,9 @@ def run_ours(args, wl):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     strong = bool(wl.get("strong"))
-    B = wl["batch"] // world if strong else wl["batch"]  # sequences this rank decodes
     if strong and wl["batch"] % world:
         raise SystemExit(f"{wl['batch']} sequences do not split evenly over {world} GPUs")
-    distinct = max(1, min(wl["layers"], int(STORE_BUDGET // layer_store_bytes(wl, B))))
+    B, distinct, _ = batched_plan(wl, world)  # sequences and distinct layer stores this rank holds
     pool, layers, q, kv_bytes = build_workload(wl, device, seed=1234 + rank, batch=B, distinct=distinct)
     L, Hq, D = wl["layers"], wl["q_heads"], wl["dim"]
     splits, scale = wl["splits"], 1 / math.sqrt(D)
@@ -368,17 +462,35 @@ def run_ours(args, wl):
     barrier()
     e2e_ms_local = e0.elapsed_time(e1) / e2e_steps
 
-    times = torch.tensor([ms_local, e2e_ms_local, dec_ms_mean], dtype=torch.float64, device=device)
+    # ---- sustained: at least 1 s of back-to-back steps with its own clock record
+    # (the timed region above may be a short burst at boost clocks; the 1 kW
+    # power cap settles the SM clock lower within about a second)
+    sus_steps = max(args.steps, int(math.ceil(args.sustained_seconds * 1e3 / max(ms_local, 1e-3))))
+    barrier()
+    sus_sampler = ClockSampler(gpu_id)
+    time.sleep(0.3)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(sus_steps):
+        step()
+    s1.record(stream)
+    barrier()
+    sus_clocks = sus_sampler.stop()
+    sus_ms_local = s0.elapsed_time(s1) / sus_steps
+    assert akv.take_device_status(device) == 0, "device status word set during the sustained region"
+
+    times = torch.tensor([ms_local, e2e_ms_local, dec_ms_mean, sus_ms_local], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, dec_ms_max = times.tolist()
+    ms, e2e_ms, dec_ms_max, sus_ms = times.tolist()
+    long_leg = None if args.no_long else long_context_leg(args, device, rank, world, local)
     peak, peak_kind = hbm_peak()
     if rank == 0:
         total_bytes = step_bytes * world
         gbs = total_bytes / (ms * 1e-3) / 1e9
         tokens = B * world / (ms * 1e-3)
         achieved = (step_bytes / L) / (dec_ms_mean * 1e-3) / 1e9
-        traffic = traffic_from_profile(f"decode_streamk_{args.workload}")
+        traffic = traffic_for(f"decode_streamk_{args.workload}") if not args.mix else None
         line = {
             "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -386,24 +498,16 @@ def run_ours(args, wl):
             "dtype": "f16 operands, f32 accumulation",
             "data": "synthetic (seeded fp16 N(0,1)" + (", 4 outlier channels per head x(+-8))" if wl.get("outliers")
                                                         else ")"),
-            "config": {
-                "workload": wl["name"], "layers": L, "q_heads": Hq, "kv_heads": wl["kv_heads"],
-                "head_dim": D, "batch_per_gpu": B, "context_tokens": wl["tokens"], "page_tokens": 16,
-                "precision_mix": {"fp16": wl["mix"][16], "int8": wl["mix"][8], "int4": wl["mix"][4],
-                                  "evicted": wl["mix"][0]},
-                "scale_group": wl["group"], "split_k": splits,
-                "kv_pool_gb_per_gpu": round(pool.nbytes / 1e9, 2),
-                "distinct_layer_stores": distinct,
-                "parallelism": f"batch-sharded x{world} (independent sequences, no collective)",
-                "l2": "inputs larger than L2 (KV pool >> 126 MB), no flush needed",
-            },
+            "config": batched_config(wl, world, B, distinct, pool.nbytes),
             "tokens_per_s": round(tokens, 1),
             "pct_of_hbm_peak": round(100 * gbs / world / peak, 2),
             "resident_bytes_per_step_per_gpu": step_bytes,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                          "kernel": "decode_streamk_kernel<128>",
-                         "traffic": traffic, "algorithmic_bytes_per_launch": step_bytes // L,
+                         "traffic": None if traffic is None else traffic["bytes_per_launch"],
+                         "traffic_source": None if traffic is None else traffic["source"],
+                         "algorithmic_bytes_per_launch": step_bytes // L,
                          "launch_ms_mean": round(dec_ms_mean, 5), "launch_ms_max_over_ranks": round(dec_ms_max, 5)},
             "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4), "tokens_per_s": round(B * world / (e2e_ms * 1e-3), 1),
@@ -412,11 +516,19 @@ def run_ours(args, wl):
                             "pinned host memory on a copy stream, overlapping the other layers' decode"},
             "gpu_launches": args.steps * L * 2,
             "clocks": clocks,
+            "sustained": {"steps": sus_steps, "seconds": round(sus_ms * sus_steps / 1e3, 3),
+                          "ms_per_step": round(sus_ms, 4),
+                          "value": round(total_bytes / (sus_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                          "tokens_per_s": round(B * world / (sus_ms * 1e-3), 1),
+                          "pct_of_hbm_peak": round(100 * total_bytes / (sus_ms * 1e-3) / 1e9 / world / peak, 2),
+                          "clocks": sus_clocks},
         }
+        if long_leg is not None:
+            line["long_context"] = long_leg
         if world == 1 and not args.no_cpu_baseline:
             cb = cpu_baseline(wl, seed=99, seconds=args.cpu_seconds)
             line["cpu_baseline"] = {"value": round(cb["gbs"], 4), "unit": "GB/s", "cores": cb["cores"],
-                                    "kind": "port", "sample": cb["sample"],
+                                    "kind": cb["kind"], "sample": cb["sample"],
                                     "tokens_per_s": round(cb["tokens_per_s"], 4)}
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -566,7 +678,10 @@ def run_pack(args, wl):
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gbs / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                      "kernel": "pack_pages_kernel<128,2048,tensor>",
-                     "traffic": traffic_from_profile("pack_pages_pack") if wl is PACK else None,
+                     "traffic": (lambda t: None if t is None else t["bytes_per_launch"])(
+                         traffic_for("pack_pages_pack") if wl is PACK else None),
+                     "traffic_source": (lambda t: None if t is None else t["source"])(
+                         traffic_for("pack_pages_pack") if wl is PACK else None),
                      "algorithmic_bytes_per_launch": read + written, "launch_ms_mean": round(ms, 5)},
         "e2e": {"value": round(layer_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": 2 * k_host.numel() * 2, "d2h_bytes_per_step": e2e_pool.nbytes,
@@ -581,37 +696,59 @@ def run_pack(args, wl):
     print(json.dumps(line), flush=True)
 
 
-def run_long(args, wl):
+def build_long_shard(wl: dict, device, rank: int, world: int):
+    """This rank's contiguous page range of the long sequence, packed into its
+    own pool.  The sequence (page precisions and K/V values) is the same for
+    every world size: precisions come from one seed, values are drawn per
+    1024-page chunk from a seed of the chunk's index."""
     import numpy as np
+    import torch
+
+    from anchorkv_b200 import pool as P
+    from anchorkv_b200.sharded import shard_range
+
+    Hkv, D = wl["kv_heads"], wl["dim"]
+    nblk = wl["tokens"] // 16
+    lo, hi = shard_range(nblk, rank, world)
+    keys = list(wl["mix"])
+    bits = np.random.default_rng(1000).choice(np.array(keys), size=(1, nblk), p=[wl["mix"][k] for k in keys])
+    bits = bits[:, lo:hi]
+    pool = P.PagePool(Hkv, D, group=wl["group"], pages={b: int((bits == b).sum()) for b in (16, 8, 4)},
+                      device=device, shuffle_seed=rank, zero=False)
+    k = torch.empty((1, Hkv, (hi - lo) * 16, D), dtype=torch.float16, device=device)
+    v = torch.empty_like(k)
+    chunk = 1024
+    for c0 in range(lo - lo % chunk, hi, chunk):
+        a, b = max(c0, lo), min(c0 + chunk, hi)
+        gen = torch.Generator(device=device).manual_seed(77 + c0 // chunk)
+        for dst in (k, v):
+            src = torch.randn((1, Hkv, chunk * 16, D), generator=gen, device=device, dtype=torch.float16)
+            dst[:, :, (a - lo) * 16:(b - lo) * 16] = src[:, :, (a - c0) * 16:(b - c0) * 16]
+    store = P.pack_dense(pool, k, v, bits, semantics="tensor")
+    del k, v
+    torch.cuda.synchronize(device)
+    return pool, store, (lo, hi)
+
+
+def long_context_leg(args, device, rank: int, world: int, local: int, wl: dict = None):
+    """One 1,048,576-token sequence split contiguously over the ranks (strong
+    scaling): every rank decodes its page range into partial states, then one
+    kernel merges them, exchanges the (max, sum, accumulator) states over NVLink
+    peer memory and merges the world's states (akv_merge_exchange); on one GPU
+    the decode's partials merge straight into the output.  Also times the NCCL
+    form (merge to states, all_gather_into_tensor, merge_states) and checks,
+    untimed, that both forms agree and that every rank holds the same output.
+    Every rank must call it; returns the measurements (max over ranks)."""
     import torch
     import torch.distributed as dist
 
     import anchorkv_b200 as akv
     from anchorkv_b200 import _lib
-    from anchorkv_b200 import pool as P
-    from anchorkv_b200.sharded import PeerExchange, shard_range
+    from anchorkv_b200.sharded import PeerExchange, sharded_packed_attention
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    wl = LONG if wl is None else wl
     Hq, Hkv, D = wl["q_heads"], wl["kv_heads"], wl["dim"]
-    nblk = wl["tokens"] // 16
-    lo, hi = shard_range(nblk, rank, world)
-    rng = np.random.default_rng(1000 + rank)
-    keys = list(wl["mix"])
-    bits = rng.choice(np.array(keys), size=(1, hi - lo), p=[wl["mix"][k] for k in keys])
-    pool = P.PagePool(Hkv, D, group=wl["group"], pages={b: int((bits == b).sum()) for b in (16, 8, 4)},
-                      device=device, shuffle_seed=rank, zero=False)
-    gen = torch.Generator(device=device).manual_seed(77 + rank)
-    k = torch.empty((1, Hkv, (hi - lo) * 16, D), dtype=torch.float16, device=device).normal_(generator=gen)
-    v = torch.empty_like(k).normal_(generator=gen)
-    store = P.pack_dense(pool, k, v, bits, semantics="tensor")
-    del k, v
+    pool, store, (lo, hi) = build_long_shard(wl, device, rank, world)
     qgen = torch.Generator(device=device).manual_seed(5)  # the same query on every rank
     q = torch.randn((1, Hq, 1, D), generator=qgen, device=device, dtype=torch.float32).half()
     kv_bytes = store.resident_bytes()
@@ -619,59 +756,94 @@ def run_long(args, wl):
     lib = _lib.load()
     ws_bytes = lib.akv_workspace_bytes(1, Hq, Hkv, D, hi - lo, 0)
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
-    state = torch.empty((1, Hq, D + 2), dtype=torch.float32, device=device)  # one rank's exchanged state
     out = torch.empty_like(q)
     exchange = PeerExchange(1, Hq, D) if world > 1 else None
     stream = torch.cuda.current_stream(device)
+    sptr = stream.cuda_stream
     status = _lib.status_word(device)
-    torch.cuda.synchronize(device)
 
     def decode():
         assert lib.akv_decode_partials(pool.arena.data_ptr(), pool.nbytes, store.table.data_ptr(),
                                        store.table.stride(0), store.seq_blocks.data_ptr(), store.max_blocks,
                                        q.data_ptr(), q.stride(0), q.stride(1), 1, Hq, Hkv, D, wl["group"], scale,
-                                       0, ws.data_ptr(), ws_bytes, status.data_ptr(), stream.cuda_stream) == 0
+                                       0, ws.data_ptr(), ws_bytes, status.data_ptr(), sptr) == 0
+
+    def combine():
+        if world == 1:  # the whole sequence is here: merge the partials straight into the output
+            assert lib.akv_merge(ws.data_ptr(), 1, Hq, D, out.data_ptr(), out.stride(0), out.stride(1), None,
+                                 status.data_ptr(), sptr) == 0
+            return
+        exchange.epoch += 1  # merge, exchange over NVLink and merge again in one kernel
+        assert lib.akv_merge_exchange(ws.data_ptr(), 1, Hq, D, exchange._peers, exchange.rank, world,
+                                      exchange.epoch, out.data_ptr(), out.stride(0), out.stride(1),
+                                      status.data_ptr(), sptr) == 0
 
     def step():
         decode()
-        if world == 1:  # the whole sequence is here: merge the partials straight into the output
-            assert lib.akv_merge(ws.data_ptr(), 1, Hq, D, out.data_ptr(), out.stride(0), out.stride(1), None,
-                                 status.data_ptr(), stream.cuda_stream) == 0
-            return
-        # merge, exchange over NVLink and merge again in one kernel (peer stores, bounded waits)
-        exchange.epoch += 1
-        assert lib.akv_merge_exchange(ws.data_ptr(), 1, Hq, D, exchange._peers, exchange.rank, world,
-                                      exchange.epoch, out.data_ptr(), out.stride(0), out.stride(1),
-                                      status.data_ptr(), stream.cuda_stream) == 0
+        combine()
+
+    def nccl_step():
+        if world == 1:
+            return akv.merge_states(akv.decode_partial_states(q, store, scale, splits=0)[None])
+        return sharded_packed_attention(q, store, scale, splits=0)
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize(device)
 
+    def events(n):
+        return [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+
+    # untimed cross-checks: the peer-memory exchange against the NCCL form, and every rank's output
+    step()
+    out_peer = out.clone()
+    out_nccl = nccl_step()
+    barrier()
+    checks = torch.zeros(2, dtype=torch.float64, device=device)
+    checks[0] = (out_peer.float() - out_nccl.float()).abs().max()
+    if world > 1:
+        every = torch.empty((world,) + tuple(out_peer.shape), dtype=out_peer.dtype, device=device)
+        dist.all_gather_into_tensor(every, out_peer)
+        checks[1] = (every.float() - every[0:1].float()).abs().max()
+        dist.all_reduce(checks, op=dist.ReduceOp.MAX)
+
+    steps = args.steps
     for _ in range(args.warmup):
         step()
     barrier()
-    gpu_id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
-    sampler = ClockSampler(gpu_id)
-    time.sleep(0.3)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for i in range(args.steps):
+    for _ in range(steps):
         step()
     t1.record(stream)
     barrier()
-    clocks = sampler.stop()
-    assert akv.take_device_status(device) == 0
-    ms_local = t0.elapsed_time(t1) / args.steps
-    # the decode kernel alone, in a separate pass (events around each launch)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ms_local = t0.elapsed_time(t1) / steps
+    ev = events(steps)  # the decode alone (events around each launch)
     for a, b in ev:
         a.record(stream)
         decode()
         b.record(stream)
     barrier()
-    dec_ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+    dec_ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    ev = events(steps)  # the combining kernel alone, each after an untimed decode
+    for a, b in ev:
+        decode()
+        a.record(stream)
+        combine()
+        b.record(stream)
+    barrier()
+    comb_ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    for _ in range(3):
+        nccl_step()
+    barrier()
+    n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0.record(stream)
+    for _ in range(steps):
+        nccl_step()
+    n1.record(stream)
+    barrier()
+    nccl_ms = n0.elapsed_time(n1) / steps
 
     # end to end: the query from pinned host memory, the output back to it
     q_host = q.cpu().pin_memory()
@@ -686,81 +858,136 @@ def run_long(args, wl):
         e2e_step()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(10, steps // 4)
     e0.record(stream)
-    for _ in range(max(10, args.steps // 4)):
+    for _ in range(e2e_steps):
         e2e_step()
     e1.record(stream)
     barrier()
-    e2e_ms_local = e0.elapsed_time(e1) / max(10, args.steps // 4)
-    totals = torch.tensor([ms_local, e2e_ms_local, dec_ms, float(kv_bytes)], dtype=torch.float64, device=device)
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    st = float(akv.take_device_status(device))
+    mx = torch.tensor([ms_local, dec_ms, comb_ms, nccl_ms, e2e_ms, st], dtype=torch.float64, device=device)
+    kv_all = torch.tensor([float(kv_bytes)], dtype=torch.float64, device=device)
     if world > 1:
-        mx = totals[:3].clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        kv_all = totals[3:].clone()
         dist.all_reduce(kv_all, op=dist.ReduceOp.SUM)
-        ms, e2e_ms, dec_ms_max = mx.tolist()
-        kv_total = kv_all.item()
-    else:
-        ms, e2e_ms, dec_ms_max = ms_local, e2e_ms_local, dec_ms
-        kv_total = float(kv_bytes)
+        exchange.close()
+    ms, dec_max, comb_max, nccl_max, e2e_max, st_max = mx.tolist()
+    assert st_max == 0, f"device status word set in the long-context leg: {int(st_max)}"
+    peak, peak_kind = hbm_peak()
+    io = 2 * q.numel() * 2
+    step_bytes = kv_all.item() + io
+    res = {
+        "workload": wl["name"], "context_tokens": wl["tokens"], "q_heads": Hq, "kv_heads": Hkv, "head_dim": D,
+        "precision_mix": {"fp16": wl["mix"][16], "int8": wl["mix"][8], "int4": wl["mix"][4]},
+        "scale_group": wl["group"], "n_gpus": world, "scaling": "strong", "steps": steps,
+        "ms_per_step": round(ms, 5), "value": round(step_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+        "tokens_per_s": round(1 / (ms * 1e-3), 1),
+        "pct_of_hbm_peak": round(100 * step_bytes / (ms * 1e-3) / 1e9 / world / peak, 2),
+        "decode_ms_max_over_ranks": round(dec_max, 5),
+        "decode_ms_rank0": round(dec_ms, 5),
+        "combine_kernel": "merge_exchange_kernel (NVLink peer stores, bounded flag waits)" if world > 1
+        else "merge_wide_kernel (local partials into the output)",
+        "combine_ms_max_over_ranks": round(comb_max, 5),
+        "nccl_variant_ms_per_step": round(nccl_max, 5),
+        "nccl_variant": "decode + merge to states + all_gather_into_tensor + merge_states" if world > 1
+        else "decode + merge to states + merge_states (no collective at one GPU)",
+        "collective_bytes_per_rank": Hq * (D + 2) * 4,
+        "check_max_abs_peer_vs_nccl": float(checks[0]), "check_max_abs_across_ranks": float(checks[1]),
+        "roofline": {"bound": "hbm", "achieved": round((kv_bytes + io) / (dec_ms * 1e-3) / 1e9, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round((kv_bytes + io) / (dec_ms * 1e-3) / 1e9 / peak, 4),
+                     "peak_source": f"{peak_kind} hbm_gbs", "kernel": "decode_streamk_kernel<128> (rank 0)",
+                     "algorithmic_bytes_per_launch": kv_bytes + io, "launch_ms_mean": round(dec_ms, 5)},
+        "e2e": {"value": round(step_bytes / (e2e_max * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(e2e_max, 5),
+                "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2},
+        "l2": "inputs larger than L2 (1.5 GB of KV over the ranks), no flush needed",
+    }
+    del pool, store, ws
+    return res
+
+
+def long_config(wl: dict, world: int) -> dict:
+    """The ``config`` of a long-context line (both arms print the same one)."""
+    return {"workload": wl["name"], "q_heads": wl["q_heads"], "kv_heads": wl["kv_heads"], "head_dim": wl["dim"],
+            "context_tokens": wl["tokens"], "page_tokens": 16,
+            "precision_mix": {"fp16": wl["mix"][16], "int8": wl["mix"][8], "int4": wl["mix"][4]},
+            "scale_group": wl["group"],
+            "parallelism": f"sequence-sharded x{world}" + (
+                ", LSE states exchanged over NVLink peer memory in the merge kernel" if world > 1 else ""),
+            "collective_bytes_per_rank": wl["q_heads"] * (wl["dim"] + 2) * 4,
+            "l2": "inputs larger than L2 (1.5 GB of KV over the ranks), no flush needed"}
+
+
+def run_long(args, wl):
+    """--workload long: the long-context leg alone, as the line's headline."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    gpu_id = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    sampler = ClockSampler(gpu_id)
+    res = long_context_leg(args, device, rank, world, local, wl)
+    clocks = sampler.stop()
     if rank == 0:
-        peak, peak_kind = hbm_peak()
-        step_bytes = kv_total + 2 * q.numel() * 2
-        gbs = step_bytes / (ms * 1e-3) / 1e9
-        achieved = (kv_bytes + 2 * q.numel() * 2) / (dec_ms * 1e-3) / 1e9
+        traffic = traffic_for("decode_streamk_long")
+        roof = dict(res["roofline"])
+        roof["traffic"] = None if traffic is None else round(traffic["bytes_per_launch"] / world)
+        roof["traffic_source"] = None if traffic is None else traffic["source"] + " (scaled by 1/n_gpus)"
         line = {
-            "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16 operands, f32 accumulation", "data": "synthetic (seeded fp16 N(0,1))",
-            "config": {"workload": wl["name"], "q_heads": Hq, "kv_heads": Hkv, "head_dim": D,
-                       "context_tokens": wl["tokens"], "page_tokens": 16,
-                       "precision_mix": {"fp16": 0.05, "int8": 0.25, "int4": 0.70}, "scale_group": wl["group"],
-                       "parallelism": f"sequence-sharded x{world}" + (
-                           ", LSE states exchanged over NVLink peer memory in the merge kernel" if world > 1 else ""),
-                       "collective_bytes_per_rank": state.numel() * 4,
-                       "l2": "inputs larger than L2 (1.5 GB of KV), no flush needed"},
-            "tokens_per_s": round(1 / (ms * 1e-3), 1),
-            "pct_of_hbm_peak": round(100 * gbs / world / peak, 2),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                         "kernel": "decode_streamk_kernel<128>",
-                         # each rank decodes 1/world of the pages: traffic scales with them
-                         "traffic": (lambda t: None if t is None else round(t / world))(
-                             traffic_from_profile("decode_streamk_long")),
-                         "launch_ms_mean": round(dec_ms, 5), "launch_ms_max_over_ranks": round(dec_ms_max, 5)},
-            "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                    "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": q.numel() * 2,
-                    "d2h_bytes_per_step": out.numel() * 2},
-            "gpu_launches": args.steps * 2,
-            "clocks": clocks,
+            "config": long_config(wl, world),
+            "tokens_per_s": res["tokens_per_s"], "pct_of_hbm_peak": res["pct_of_hbm_peak"],
+            "roofline": roof, "e2e": res["e2e"], "long_context": res,
+            "gpu_launches": args.steps * 2, "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
-        exchange.close()
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
 
 
-def run_reference(args, wl):
+def run_reference(args, wl, long=False):
+    """The reference arm: the reference's own CPU decode path (``cpu_baseline``)
+    on the host cores, same metric, unit and config as this repository's arm.
+    A step is a bounded sample (one sequence-layer decode call of the workload,
+    or a 65,536-token slice of the long sequence); ``value`` is the sample's
+    resident-KV GB/s and tokens/s is extrapolated to the full workload.  Under
+    torchrun only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     per_step = max(0.02, args.cpu_seconds / max(1, args.steps))
     cb = cpu_baseline(wl, seed=99, seconds=per_step * args.steps, calls_min=args.steps + args.warmup)
+    if long:
+        config = long_config(wl, world)
+        scaling = "strong"
+    else:
+        B, distinct, arena = batched_plan(wl, world)
+        config = batched_config(wl, world, B, distinct, arena)
+        scaling = "strong" if wl.get("strong") else "weak"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(cb["gbs"], 4), "unit": "GB/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(cb["seconds_per_call"] * wl["layers"] * wl["batch"] * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "calls_timed": cb["calls"],
+        "ms_per_step": round(cb["seconds_per_call"] * 1e3, 3),
+        "ms_per_full_step_extrapolated": round(cb["seconds_per_call"] * cb["calls_per_step"] * 1e3, 1),
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
         "dtype": "f16 operands (torch CPU SDPA)", "data": "synthetic (seeded fp16 N(0,1))",
-        "config": {"workload": wl["name"], "layers": wl["layers"], "q_heads": wl["q_heads"],
-                   "kv_heads": wl["kv_heads"], "head_dim": wl["dim"], "batch_per_gpu": wl["batch"],
-                   "context_tokens": wl["tokens"], "scale_group": wl["group"]},
+        "config": config,
         "tokens_per_s": round(cb["tokens_per_s"], 4),
-        "cpu_baseline": {"value": round(cb["gbs"], 4), "unit": "GB/s", "cores": cb["cores"], "kind": "port",
+        "cpu_baseline": {"value": round(cb["gbs"], 4), "unit": "GB/s", "cores": cb["cores"], "kind": cb["kind"],
                          "sample": cb["sample"]},
         "e2e": {"value": round(cb["gbs"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "step_definition": "one decode call of one sequence-layer (a bounded sample of the full step)",
     }
     print(json.dumps(line), flush=True)
 
@@ -860,6 +1087,10 @@ def main():
                     help="profiling: every page of a batched workload in this one precision")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="seconds of CPU timing for the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline (profiling runs)")
+    ap.add_argument("--no-long", action="store_true",
+                    help="skip the long-context leg of the batched/large runs (profiling runs)")
+    ap.add_argument("--sustained-seconds", type=float, default=1.2,
+                    help="seconds of back-to-back steps in the line's sustained record")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -881,7 +1112,7 @@ def main():
         return
     if args.workload == "long":
         if args.impl == "reference":
-            run_reference(args, dict(LONG, layers=1, batch=1, splits=0))
+            run_reference(args, dict(LONG, layers=1, batch=1, splits=0), long=True)
         else:
             run_long(args, LONG)
         return

@@ -28,6 +28,8 @@ _f32 = ctypes.c_float
 PROTOTYPES = {
     "akv_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "akv_abi_version": (ctypes.c_int, []),
+    "akv_status_alloc": (ctypes.c_int, [ctypes.POINTER(_c_p), ctypes.POINTER(_c_p)]),
+    "akv_status_free": (ctypes.c_int, [_c_p]),
     "akv_record_bytes": (_i64, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "akv_quantize": (ctypes.c_int, [_c_p, ctypes.c_int, _i64, _i64, ctypes.c_int, ctypes.c_int,
                                     _c_p, _c_p, _c_p]),
@@ -123,11 +125,50 @@ def stream_of(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+DEV_BITS = {DEV_BAD_DESCRIPTOR: "a page descriptor outside the arena or misaligned (page skipped)",
+            DEV_TIMEOUT: "a bounded wait that gave up (a bulk copy or a peer's exchange flag)"}
+
+
+class StatusWord:
+    """The int32 word a device's kernels OR their AKV_DEV_* error bits into.
+
+    It lives in mapped pinned host memory (akv_status_alloc): kernels write it
+    through its device address (:meth:`data_ptr`), the host reads it through
+    its host address with no copy and no synchronisation, so every API call
+    can check it before launching.  A kernel's bits are visible once it has
+    finished."""
+
+    def __init__(self, index: int):
+        import torch
+
+        host, dev = ctypes.c_void_p(), ctypes.c_void_p()
+        with torch.cuda.device(index):
+            call("akv_status_alloc", ctypes.byref(host), ctypes.byref(dev))
+        self.index = index
+        self._dev = dev.value
+        self._word = ctypes.c_int32.from_address(host.value)
+
+    def data_ptr(self) -> int:
+        return self._dev
+
+    @property
+    def value(self) -> int:
+        return self._word.value
+
+    def clear(self) -> None:
+        self._word.value = 0
+
+
+def describe_status(bits: int) -> str:
+    parts = [text for bit, text in DEV_BITS.items() if bits & bit]
+    return "; ".join(parts) or f"unknown device status bits {bits:#x}"
+
+
 _status = {}
 
 
-def status_word(device):
-    """The per-device int32 word kernels OR their error bits into."""
+def status_word(device) -> StatusWord:
+    """The device's status word (one per device, created on first use)."""
     word = _status.get(device)  # fast path: the device object seen before
     if word is not None:
         return word
@@ -136,17 +177,42 @@ def status_word(device):
     dev = torch.device(device)
     key = dev.index if dev.index is not None else torch.cuda.current_device()
     if key not in _status:
-        _status[key] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key))
+        _status[key] = StatusWord(key)
     if dev.index is not None:  # "cuda" without an index follows the current device: not cached by name
         _status[device] = _status[key]
     return _status[key]
+
+
+def raise_pending(device) -> None:
+    """Raise :class:`KernelError` if a kernel that has finished on ``device``
+    reported an error (and clear the word, so the call after this one runs).
+
+    The reference signals bad input with exceptions from host code; here the
+    page table and exchange flags are read on the device, so their errors
+    surface on the next API call instead of as silent zeros."""
+    word = status_word(device)
+    bits = word.value
+    if bits:
+        word.clear()
+        raise KernelError(f"an earlier kernel on cuda:{word.index} reported: {describe_status(bits)}")
+
+
+def status_ptr(device) -> int:
+    """Device address of ``device``'s status word for a launch, after raising
+    any error a finished kernel already reported there (:func:`raise_pending`)."""
+    word = status_word(device)
+    if word.value:
+        raise_pending(device)
+    return word.data_ptr()
 
 
 def take_device_status(device=None) -> int:
     """Synchronise, return and clear the device error bits (0 = no error)."""
     import torch
 
-    word = status_word(device if device is not None else torch.cuda.current_device())
-    value = int(word.item())
-    word.zero_()
+    dev = device if device is not None else torch.cuda.current_device()
+    word = status_word(dev)
+    torch.cuda.synchronize(word.index)
+    value = word.value
+    word.clear()
     return value

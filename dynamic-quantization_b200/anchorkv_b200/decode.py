@@ -94,7 +94,7 @@ def packed_attention(query, layer, scale, splits=4, *, out=None):
               None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks,
               query.data_ptr(), query.stride(0), query.stride(1), batch, heads, layer.heads, layer.dim,
               layer.group, float(scale), splits, out.data_ptr(), out.stride(0), out.stride(1),
-              ws.data_ptr(), ws.numel(), _lib.status_word(dev).data_ptr(), stream)
+              ws.data_ptr(), ws.numel(), _lib.status_ptr(dev), stream)
     return out
 
 
@@ -116,7 +116,7 @@ def decode_partial_states(query, layer, scale, splits=0):
     stream = _lib.stream_of(dev)
     ws = _workspace(dev, nbytes, stream)
     state = torch.empty((batch, heads, layer.dim + 2), dtype=torch.float32, device=dev)
-    status = _lib.status_word(dev).data_ptr()
+    status = _lib.status_ptr(dev)
     _lib.call("akv_decode_partials", arena.data_ptr(), arena_bytes, table.data_ptr(), table.stride(0),
               None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks, query.data_ptr(),
               query.stride(0), query.stride(1), batch, heads, layer.heads, layer.dim, layer.group,

@@ -247,7 +247,7 @@ def pack_dense(pool: PagePool, key: torch.Tensor, value: torch.Tensor, block_bit
     sem = _lib.SEM_TENSOR if semantics == "tensor" else _lib.SEM_PAGE
     _lib.call("akv_pack_pages", key.data_ptr(), value.data_ptr(), heads * padded * dim, padded * dim,
               nblk, batch * nblk, dst.data_ptr(), pool.arena.data_ptr(), pool.nbytes, heads, dim,
-              pool.group, sem, _lib.status_word(dev).data_ptr(), _lib.stream_of(dev))
+              pool.group, sem, _lib.status_ptr(dev), _lib.stream_of(dev))
     out = PagedBatch(pool, batch, nblk)
     if visible is not None:
         desc = np.where(np.asarray(visible, bool).reshape(batch, nblk), desc, 0)

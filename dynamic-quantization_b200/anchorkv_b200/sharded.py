@@ -122,7 +122,7 @@ class PeerExchange:
         if out is None:
             out = torch.empty_like(query)
         stream = _lib.stream_of(dev)
-        status = _lib.status_word(dev).data_ptr()
+        status = _lib.status_ptr(dev)
         _lib.call("akv_decode_partials", arena.data_ptr(), arena_bytes, table.data_ptr(), table.stride(0),
                   None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks, query.data_ptr(),
                   query.stride(0), query.stride(1), self.batch, self.q_heads, local_store.heads, self.dim,

@@ -15,7 +15,30 @@ extern "C" const char *akv_status_string(int status) {
 }
 
 // 3: V payloads stored in the bank-swizzled byte order (records of version 2 read differently).
-extern "C" int akv_abi_version(void) { return 3; }
+// 4: exchange buffers hold both epoch parities (akv_exchange_bytes doubled).
+extern "C" int akv_abi_version(void) { return 4; }
+
+// The status word in mapped pinned host memory: kernels write it through the
+// device address, the host reads it through the host address with no copy or
+// synchronisation.
+extern "C" int akv_status_alloc(void **host_ptr, void **dev_ptr) {
+  if (!host_ptr || !dev_ptr) return AKV_ERR_INVALID;
+  void *h = nullptr;
+  if (cudaHostAlloc(&h, 64, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) return AKV_ERR_CUDA;
+  void *d = nullptr;
+  if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) {
+    cudaFreeHost(h);
+    return AKV_ERR_CUDA;
+  }
+  *(volatile int32_t *)h = 0;
+  *host_ptr = h;
+  *dev_ptr = d;
+  return AKV_OK;
+}
+
+extern "C" int akv_status_free(void *host_ptr) {
+  return host_ptr && cudaFreeHost(host_ptr) == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+}
 
 extern "C" int64_t akv_record_bytes(int head_dim, int group, int mode) {
   if (head_dim <= 0 || group <= 0 || (16 * head_dim) % group) return -1;

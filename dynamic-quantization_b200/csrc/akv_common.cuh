@@ -239,8 +239,18 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
   return __float2bfloat16_rn(x);
 }
 
+// Record error bits in the caller's status word.  The word may be device
+// memory or mapped pinned host memory (the Python layer keeps it there, so the
+// host reads it without synchronising), so this is a plain read-OR-write, not
+// an atomic (atomics on host memory are not portable across PCIe hosts): two
+// different bits raised at the same moment may leave only one of them, but the
+// word is nonzero after any error.  Only error paths call it.
 __device__ __forceinline__ void set_status(int32_t *status, int bits) {
-  if (status) atomicOr(status, bits);
+  if (!status) return;
+  volatile int32_t *w = status;
+  const int32_t v = *w;
+  if ((v & bits) != bits) *w = v | bits;
+  __threadfence_system();
 }
 
 // ----------------------------------------------------------- quantizer core

@@ -865,38 +865,48 @@ __global__ void __launch_bounds__(128) merge_rows_kernel(const int32_t *__restri
 }
 
 // Fold contributors w, w + stride, ... (<= w_end) of `item`, query head n of its
-// group, into (m, l, acc): every load of a contributor is issued before its
-// weight is tested (two in flight per loop trip), and each contributor's first
-// item advances incrementally.
+// group, into (m, l, acc).  Contributors are loaded CB at a time, all loads of a
+// batch issued before any is combined, so a warp pays one L2 round trip per CB
+// contributors; each contributor's first item advances incrementally.
 template <int D>
 __device__ __forceinline__ void fold_partials(const MergeGeom &g, int item, int n, int w, int w_end, int stride,
                                               int lane, float &m, float &l, float (&acc)[D / 32]) {
-  constexpr int PS = D + 4, VEC = D / 32;
+  constexpr int PS = D + 4, VEC = D / 32, CB = 4;
   if (w > w_end) return;
   int first = w * g.range / g.mb, rem = w * g.range - first * g.mb;
   const int step = stride * g.range, sq = step / g.mb, sr = step - sq * g.mb;
-#pragma unroll 2
-  for (; w <= w_end; w += stride) {
-    const float *pr = g.partials + ((int64_t)(w * g.smax + (item - first)) * g.slot_heads + n) * PS;
-    const float mw = __ldcg(pr + D), lw = __ldcg(pr + D + 1);
-    float a[VEC];
-    if constexpr (VEC == 4) {
-      const float4 v = __ldcg(reinterpret_cast<const float4 *>(pr) + lane);
-      a[0] = v.x, a[1] = v.y, a[2] = v.z, a[3] = v.w;
-    } else {
-      const float2 v = __ldcg(reinterpret_cast<const float2 *>(pr) + lane);
-      a[0] = v.x, a[1] = v.y;
-    }
-    if (mw != -INFINITY) {  // an empty share weighs 0 (triton_decode.py:78)
-      const float top = fmaxf(m, mw);
-      const float c = ex2(m - top), e = ex2(mw - top);
-      l = l * c + e * lw;
+  for (; w <= w_end; w += CB * stride) {
+    float mw[CB], lw[CB], a[CB][VEC];
 #pragma unroll
-      for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * c + e * a[i];
+    for (int j = 0; j < CB; ++j) {
+      mw[j] = -INFINITY, lw[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) a[j][i] = 0.f;
+      if (w + j * stride <= w_end) {
+        const float *pr =
+            g.partials + ((int64_t)((w + j * stride) * g.smax + (item - first)) * g.slot_heads + n) * PS;
+        mw[j] = __ldcg(pr + D), lw[j] = __ldcg(pr + D + 1);
+        if constexpr (VEC == 4) {
+          const float4 v = __ldcg(reinterpret_cast<const float4 *>(pr) + lane);
+          a[j][0] = v.x, a[j][1] = v.y, a[j][2] = v.z, a[j][3] = v.w;
+        } else {
+          const float2 v = __ldcg(reinterpret_cast<const float2 *>(pr) + lane);
+          a[j][0] = v.x, a[j][1] = v.y;
+        }
+        first += sq, rem += sr;
+        if (rem >= g.mb) rem -= g.mb, ++first;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < CB; ++j) {
+      if (mw[j] == -INFINITY) continue;  // an empty share (or past w_end) weighs 0 (triton_decode.py:78)
+      const float top = fmaxf(m, mw[j]);
+      const float c = ex2(m - top), e = ex2(mw[j] - top);
+      l = l * c + e * lw[j];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) acc[i] = acc[i] * c + e * a[j][i];
       m = top;
     }
-    first += sq, rem += sr;
-    if (rem >= g.mb) rem -= g.mb, ++first;
   }
 }
 
@@ -963,9 +973,19 @@ __global__ void __launch_bounds__(1024) merge_wide_kernel(const int32_t *__restr
 // stores before it waits, so no CTA waits on one that cannot run.
 //
 // Exchange buffer of one rank (akv_exchange_bytes): fp32 states
-// [world][rows][D+2] (slot r holds rank r's state of every row), then uint32
-// flags [world][rows] (flag [r][row] = the epoch of the last call whose rank-r
+// [2][world][rows][D+2] (slot [e & 1][r] holds rank r's state of every row for
+// the calls of epoch parity e & 1), then uint32 flags [2][world][rows] (flag
+// [e & 1][r][row] = the epoch of the last call of that parity whose rank-r
 // state of the row has landed).  Buffers start zeroed; epochs start at 1.
+//
+// Two parities make consecutive calls safe without any extra handshake: rank
+// A's call e + 2 writes the parity-(e & 1) slots again only after its call
+// e + 1 finished, which needed every peer's call-(e + 1) state of every row,
+// and a peer publishes e + 1 only after its whole call-e grid (every read of
+// the parity-(e & 1) slots) has completed: its decode of e + 1 waits for that
+// grid, and its exchange of e + 1 waits for the decode.  With one slot a fast
+// rank's call e + 1 could overwrite a state (and move the flag past e) that a
+// slower rank was still waiting for or reading.
 constexpr int kMaxPeers = 8;
 struct PeerBuffers {
   void *buf[kMaxPeers];
@@ -1025,10 +1045,11 @@ __global__ void __launch_bounds__(1024) merge_exchange_kernel(const int32_t *__r
     for (int i = 0; i < VEC; ++i) num[i] += e * sm_acc[k][VEC * lane + i];
   }
   const int rows = gridDim.x * gridDim.y, row = b * q_heads + h;
-  const int64_t flag_offset = (int64_t)world * rows * RS;  // in floats
-  // (2) publish to every rank, this one included
+  const int64_t par = epoch & 1u;
+  const int64_t flag_offset = 2ll * world * rows * RS;  // in floats: the flags follow both parities' states
+  // (2) publish to every rank, this one included, into this epoch parity's slots
   for (int pr = 0; pr < world; ++pr) {
-    float *st = reinterpret_cast<float *>(peers.buf[pr]) + ((int64_t)rank * rows + row) * RS;
+    float *st = reinterpret_cast<float *>(peers.buf[pr]) + ((par * world + rank) * rows + row) * RS;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) st[VEC * lane + i] = num[i];
     if (lane == 0) st[D] = top, st[D + 1] = den;
@@ -1037,11 +1058,13 @@ __global__ void __launch_bounds__(1024) merge_exchange_kernel(const int32_t *__r
   __syncwarp();
   if (lane < world)
     st_release_sys(reinterpret_cast<uint32_t *>(reinterpret_cast<float *>(peers.buf[lane]) + flag_offset) +
-                       (int64_t)rank * rows + row,
+                       (par * world + rank) * rows + row,
                    epoch);
   // (3) bounded wait for every rank's state of this row (lane q watches rank q)
-  const float *mine = reinterpret_cast<const float *>(peers.buf[rank]);
-  const uint32_t *flags = reinterpret_cast<const uint32_t *>(mine + flag_offset);
+  const float *mine = reinterpret_cast<const float *>(peers.buf[rank]) + par * world * rows * RS;
+  const uint32_t *flags =
+      reinterpret_cast<const uint32_t *>(reinterpret_cast<const float *>(peers.buf[rank]) + flag_offset) +
+      par * world * rows;
   bool ok = true;
   if (lane < world) {
     const uint64_t t0 = globaltimer();
@@ -1324,7 +1347,7 @@ extern "C" int64_t akv_exchange_bytes(int32_t world, int32_t batch, int32_t q_he
   if (world <= 0 || world > kMaxPeers || batch <= 0 || q_heads <= 0 || (head_dim != 64 && head_dim != 128))
     return -1;
   const int64_t rows = (int64_t)batch * q_heads;
-  return world * rows * (head_dim + 2) * 4 + world * rows * 4;
+  return 2 * (world * rows * (head_dim + 2) * 4 + world * rows * 4);  // both epoch parities
 }
 
 extern "C" int akv_merge_exchange(const void *workspace, int32_t batch, int32_t q_heads, int32_t head_dim,
@@ -1447,12 +1470,14 @@ extern "C" int akv_packed_attention_static(const void *arena, int64_t arena_byte
                                            int32_t splits, void *out, int64_t out_batch_stride,
                                            int64_t out_head_stride, int32_t *dev_status, void *stream) {
   if (!out) return AKV_ERR_INVALID;
-  int64_t need = akv_workspace_bytes(batch, q_heads, kv_heads, head_dim, max_blocks, splits);
-  if (need <= 0) return AKV_ERR_INVALID;
+  // The same plan akv_workspace_bytes sizes, with its own status on failure
+  // (unsupported head_dim, invalid geometry, a CUDA query error), as
+  // akv_packed_attention would report it.
+  akv::Plan pl;
+  if (int st = akv::make_plan(batch, q_heads, kv_heads, head_dim, max_blocks, splits, &pl)) return st;
+  int64_t need = pl.bytes;
   if (need > akv::kStaticScratchBytes) {  // try exactly `splits` pieces per item, without the finer cut
-    akv::Plan pl;
-    if (akv::make_plan(batch, q_heads, kv_heads, head_dim, max_blocks, splits, &pl, false) != AKV_OK)
-      return AKV_ERR_INVALID;
+    if (int st = akv::make_plan(batch, q_heads, kv_heads, head_dim, max_blocks, splits, &pl, false)) return st;
     if (pl.bytes > akv::kStaticScratchBytes) return AKV_ERR_SCRATCH;
     need = akv::kStaticScratchBytes;  // the decode picks the decomposition that fits
   }
@@ -1460,7 +1485,11 @@ extern "C" int akv_packed_attention_static(const void *arena, int64_t arena_byte
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return AKV_ERR_CUDA;
   void *scratch = nullptr;
   {
-    // First call on a device: look up the array's device address with that device current.
+    // First call on a device: look up the array's device address with that
+    // device current.  The address is kept for the life of the process: a
+    // cudaDeviceReset on that device unloads this module's copy of the array,
+    // after which the kept address is stale and this entry point must not be
+    // called on that device again.
     std::lock_guard<std::mutex> lock(g_static_mu);
     if (!g_static_ptr[dev]) {
       void *p = nullptr;

@@ -49,7 +49,11 @@ extern "C" {
 #define AKV_ERR_CUDA 3        /* CUDA error when launching */
 #define AKV_ERR_SCRATCH 4     /* request larger than akv_packed_attention_static's fixed scratch */
 
-/* Bits a kernel ORs into the optional device status word (int32, caller owned). */
+/* Bits a kernel ORs into the optional status word (int32, caller owned; device
+ * memory, or mapped pinned host memory from akv_status_alloc so that the host
+ * can read it without synchronising).  Kernels set bits with a plain
+ * read-OR-write, not an atomic: two different bits raised at the same moment
+ * may leave only one of them, but the word is nonzero after any error. */
 #define AKV_DEV_BAD_DESCRIPTOR 1 /* descriptor outside the arena or misaligned; page skipped */
 #define AKV_DEV_TIMEOUT 2        /* a bounded wait on a bulk copy gave up */
 
@@ -73,6 +77,15 @@ const char *akv_status_string(int status);
 
 /* ABI version, bumped on any incompatible change. */
 int akv_abi_version(void);
+
+/* A status word in mapped pinned host memory (64 bytes, zeroed): kernels get
+ * `*dev_ptr`, the host reads `*host_ptr` with no copy or synchronisation (the
+ * bits of a kernel are visible once it has finished).  No counterpart in the
+ * reference, which raises exceptions from host code only; this is how the
+ * Python layer turns device-side errors (AKV_DEV_*) into exceptions on the
+ * next call.  Free with akv_status_free. */
+int akv_status_alloc(void **host_ptr, void **dev_ptr);
+int akv_status_free(void *host_ptr);
 
 /* Bytes of one (page, head) record for a mode (0 for AKV_MODE_SKIP); -1 for an
  * unsupported geometry.  Replaces the byte accounting of QuantizedPage.nbytes
@@ -171,8 +184,8 @@ int akv_merge_states(const float *states, int32_t n, int32_t batch, int32_t q_he
                      int64_t out_head_stride, void *stream);
 
 /* Bytes of one rank's exchange buffer for akv_merge_exchange (-1 if invalid):
- * fp32 states [world][batch * q_heads][head_dim + 2] then uint32 flags
- * [world][batch * q_heads].  world <= 8. */
+ * fp32 states [2][world][batch * q_heads][head_dim + 2] then uint32 flags
+ * [2][world][batch * q_heads], the leading 2 being the epoch parity.  world <= 8. */
 int64_t akv_exchange_bytes(int32_t world, int32_t batch, int32_t q_heads, int32_t head_dim);
 
 /* Cross-GPU merge over peer memory for one sequence split over `world` GPUs
@@ -185,7 +198,12 @@ int64_t akv_exchange_bytes(int32_t world, int32_t batch, int32_t q_heads, int32_
  *   peer_buffers[r]: rank r's exchange buffer as mapped in this process
  *     (akv_ipc_alloc / akv_ipc_open), zeroed before the first call;
  *   epoch: 1 for the first call on these buffers, +1 for each following call,
- *     the same on every rank.  Every rank must make the same calls. */
+ *     the same on every rank.  Every rank must make the same calls.
+ * Calls of even and odd epochs use separate halves of the buffers, so a rank
+ * may run one call ahead of a slower peer: it writes epoch e + 1's states into
+ * the other half while the peer still reads epoch e's, and it cannot reach
+ * epoch e + 2 before every peer has published e + 1 (which each does only
+ * after finishing its call e). */
 int akv_merge_exchange(const void *workspace, int32_t batch, int32_t q_heads, int32_t head_dim,
                        void *const *peer_buffers, int32_t rank, int32_t world, uint32_t epoch, void *out,
                        int64_t out_batch_stride, int64_t out_head_stride, int32_t *dev_status,
@@ -226,7 +244,11 @@ int akv_packed_attention(const void *arena, int64_t arena_bytes, const int64_t *
  * requests whose partial states exceed 8 MiB even then return AKV_ERR_SCRATCH.
  * The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture.  All calls on a device share the array and it keeps the
+ * any stream capture.  The address is kept for the life of the process, so
+ * after a cudaDeviceReset of that device (which unloads the library's copy of
+ * the array) this entry point must not be called on it again.  Failures of
+ * the plan (AKV_ERR_INVALID / AKV_ERR_UNSUPPORTED / AKV_ERR_CUDA) are the ones
+ * akv_packed_attention reports.  All calls on a device share the array and it keeps the
  * last call's contents (each call rewrites what it reads, so nothing needs
  * clearing); calls whose kernels overlap on the GPU race on it. */
 int akv_packed_attention_static(const void *arena, int64_t arena_bytes, const int64_t *table,

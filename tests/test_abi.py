@@ -28,7 +28,7 @@ def test_library_exports_declared_symbol(name):
 
 def test_host_helpers_need_no_gpu():
     lib = _lib.load()
-    assert lib.akv_abi_version() == 3
+    assert lib.akv_abi_version() == 4
     assert _lib.status_string(_lib.ERR_INVALID).startswith("invalid")
     for dim in (64, 128):
         for group in (32, 64, 128, 16 * dim):
@@ -49,3 +49,21 @@ def test_invalid_arguments_are_rejected_before_any_launch():
         _lib.call("akv_merge", None, 1, 1, 128, None, 0, 0, None, None, None)
     with pytest.raises(ValueError):
         _lib.call("akv_merge_states", None, 2, 1, 1, 128, None, 0, 0, None)
+
+
+def test_allocation_free_entry_reports_the_workspace_entrys_status():
+    """akv_packed_attention_static returns the plan's own status (unsupported
+    head_dim, inconsistent heads) as akv_packed_attention does; both checks
+    come before any CUDA call, so this runs without a GPU.  The non-null
+    pointers are never dereferenced."""
+    lib = _lib.load()
+    fake = ctypes.c_void_p(0x1000)
+
+    def static(batch, q_heads, kv_heads, head_dim):
+        return lib.akv_packed_attention_static(fake, 1 << 20, fake, 64, None, 64, fake, 0, head_dim, batch,
+                                               q_heads, kv_heads, head_dim, 16 * head_dim, 1.0, 4, fake, 0,
+                                               head_dim, None, None)
+
+    assert static(1, 16, 8, 96) == _lib.ERR_UNSUPPORTED
+    assert static(1, 12, 8, 128) == _lib.ERR_INVALID  # 12 query heads over 8 KV heads
+    assert lib.akv_workspace_bytes(1, 16, 8, 96, 64, 4) == -1

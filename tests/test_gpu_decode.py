@@ -188,9 +188,15 @@ def test_out_of_arena_descriptor_is_skipped_and_reported(cuda):
     assert akv.take_device_status(cuda) == 0
     store.table[0, 2] = P.encode(16, 16, pool.nbytes + 4096)  # beyond the arena: bounds check skips it
     bad = akv.packed_attention(q, store, 0.125)
-    assert akv.take_device_status(cuda) & 1
+    torch.cuda.synchronize(cuda)  # the kernel has finished: its report is visible to the host
+    with pytest.raises(akv.KernelError, match="outside the arena"):
+        akv.packed_attention(q, store, 0.125)  # the next call raises before it launches
+    assert akv.take_device_status(cuda) == 0  # raising cleared the word
     torch.testing.assert_close(bad, expect)
     assert not torch.equal(good, expect)
+    bad_again = akv.packed_attention(q, store, 0.125)
+    assert akv.take_device_status(cuda) & 1  # the synchronising read reports it as well
+    torch.testing.assert_close(bad_again, expect)
 
 
 def _batch_store(cuda, batch, tokens, hq=16, hkv=8, dim=128, seed=41):

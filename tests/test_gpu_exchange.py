@@ -90,21 +90,29 @@ def test_exchange_wait_runs_out_and_reports(cuda):
     _decode(store, qd, ws)
     _lib.call("akv_merge_exchange", ws.data_ptr(), 1, HQ, D, peers, 0, 2, 1, out.data_ptr(), out.stride(0),
               out.stride(1), _lib.status_word(cuda).data_ptr(), torch.cuda.current_stream(cuda).cuda_stream)
-    assert akv.take_device_status(cuda) & 2  # AKV_DEV_TIMEOUT
+    torch.cuda.synchronize(cuda)
+    with pytest.raises(akv.KernelError, match="bounded wait"):  # the API's next call reports it
+        akv.packed_attention(qd, store, 0.088)
+    assert akv.take_device_status(cuda) == 0  # raising cleared the word
     assert (out == 0).all()  # nothing merged
     assert float(torch.ones(4, device=cuda).sum()) == 4.0  # the context still works
     for ptr in (own, silent):
         _lib.call("akv_ipc_free", ctypes.c_void_p(ptr))
 
 
-def _rank_main(rank, world, port, queue):
+def _rank_main(rank, world, port, queue, epochs=3, delay_rank=None):
+    """One rank: its shard of the sequence, ``epochs`` back-to-back calls of
+    PeerExchange.attention and one of the NCCL all-gather form.  Rank
+    ``delay_rank`` sleeps on the host before most of its calls, so the other
+    rank runs ahead by up to one call and waits for it inside the kernel."""
     try:
         os.environ["NCCL_NVLS_ENABLE"] = "0"
         import datetime
+        import time
 
         import torch.distributed as dist
 
-        from anchorkv_b200.sharded import PeerExchange, shard_range
+        from anchorkv_b200.sharded import PeerExchange, shard_range, sharded_packed_attention
 
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
@@ -113,18 +121,24 @@ def _rank_main(rank, world, port, queue):
         k, v, q, bits = _sequence()
         lo, hi = shard_range(PAGES, rank, world)
         store = _store(dev, k, v, bits, lo, hi)
+        qd = q.to(dev)
         ex = PeerExchange(1, HQ, D)
-        outs = [ex.attention(q.to(dev), store, 0.088).float().cpu() for _ in range(3)]
+        outs = []
+        for e in range(epochs):
+            if rank == delay_rank and e % 4 != 3:
+                time.sleep(0.002 * (1 + e % 3) ** 2)  # 2, 8 or 18 ms of host delay before the launches
+            outs.append(ex.attention(qd, store, 0.088))
+        outs = [o.float().cpu() for o in outs]
+        nccl = sharded_packed_attention(qd, store, 0.088).float().cpu()
         status = akv.take_device_status(dev)
         ex.close()
         dist.destroy_process_group()
-        queue.put((rank, status, [o.numpy() for o in outs]))
+        queue.put((rank, status, [o.numpy() for o in outs], nccl.numpy()))
     except Exception as exc:  # reported to the parent, which fails the test
-        queue.put((rank, -1, repr(exc)))
+        queue.put((rank, -1, repr(exc), None))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_rank_exchange_against_oracle():
+def _run_ranks(world, **kw):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
@@ -132,19 +146,49 @@ def test_two_rank_exchange_against_oracle():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, queue), kwargs=kw) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
     for _ in procs:
-        rank, status, outs = queue.get(timeout=240)
-        results[rank] = (status, outs)
+        rank, status, outs, nccl = queue.get(timeout=240)
+        results[rank] = (status, outs, nccl)
     for p in procs:
         p.join(timeout=60)
     assert all(results[r][0] == 0 for r in results), results
+    return results
+
+
+def _oracle():
     k, v, q, bits = _sequence()
-    oracle = paged_decode_f64(q[:, :, 0].numpy(), k.numpy(), v.numpy(), bits, 0.088, group=2048)
+    return paged_decode_f64(q[:, :, 0].numpy(), k.numpy(), v.numpy(), bits, 0.088, group=2048)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_exchange_against_oracle():
+    results = _run_ranks(2)
+    oracle = _oracle()
     for r in (0, 1):
         for out in results[r][1]:
             np.testing.assert_allclose(out.reshape(-1), oracle.reshape(-1), atol=2e-3, rtol=1e-2)
     np.testing.assert_array_equal(results[0][1][0], results[1][1][0])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_rank_exchange_with_a_delayed_rank():
+    """Twelve back-to-back epochs while rank 1 sleeps on the host before most
+    calls: rank 0's kernels run up to one call ahead and wait for rank 1's
+    states inside the kernel.  The epoch-parity halves of the exchange buffers
+    keep every call's states apart, so no wait runs out (status 0 on both
+    ranks), every output is within tolerance of the oracle, both ranks agree
+    bit for bit, and the NCCL all-gather form gives the same result."""
+    results = _run_ranks(2, epochs=12, delay_rank=1)
+    oracle = _oracle()
+    for r in (0, 1):
+        status, outs, nccl = results[r]
+        assert len(outs) == 12
+        for out in outs:
+            np.testing.assert_allclose(out.reshape(-1), oracle.reshape(-1), atol=2e-3, rtol=1e-2)
+            np.testing.assert_array_equal(out, outs[0])  # the same inputs every epoch
+        np.testing.assert_allclose(nccl.reshape(-1), outs[0].reshape(-1), atol=1e-3, rtol=1e-3)
+    np.testing.assert_array_equal(results[0][1][-1], results[1][1][-1])

@@ -191,3 +191,45 @@ def test_cpu_tensors_are_refused_by_the_kernels():
         akv.quantize_tensor(torch.randn(4, 8), CacheMode.INT8, group_size=16)
     with pytest.raises(ValueError, match="CUDA"):
         akv.pack_page(torch.randn(2, 16, 64), 4)
+
+
+class _HostWord:
+    """A status word in plain host memory standing in for the mapped pinned one."""
+
+    def __init__(self, index):
+        import ctypes
+
+        self.index = index
+        self._buf = ctypes.c_int32(0)
+
+    def data_ptr(self):
+        import ctypes
+
+        return ctypes.addressof(self._buf)
+
+    @property
+    def value(self):
+        return self._buf.value
+
+    def clear(self):
+        self._buf.value = 0
+
+    def set(self, bits):
+        self._buf.value |= bits
+
+
+def test_reported_device_errors_raise_on_the_next_call(monkeypatch):
+    from anchorkv_b200 import _lib
+
+    word = _HostWord(5)
+    monkeypatch.setitem(_lib._status, "fake-device", word)
+    assert _lib.status_ptr("fake-device") == word.data_ptr()  # clean: no raise
+    word.set(_lib.DEV_BAD_DESCRIPTOR)  # a kernel skipped a bad page
+    with pytest.raises(akv.KernelError, match="cuda:5 reported: a page descriptor outside the arena"):
+        _lib.status_ptr("fake-device")
+    assert word.value == 0  # raising cleared it: the call after runs
+    assert _lib.status_ptr("fake-device") == word.data_ptr()
+    word.set(_lib.DEV_BAD_DESCRIPTOR | _lib.DEV_TIMEOUT)
+    with pytest.raises(akv.KernelError, match="misaligned.*bounded wait"):
+        _lib.raise_pending("fake-device")
+    assert _lib.describe_status(8).startswith("unknown")
