@@ -237,7 +237,7 @@ class PagedLayer:
         dst_t = torch.tensor(dst, dtype=torch.int64).to(dev, non_blocking=False)
         _lib.call("akv_repack_pages", src_t.data_ptr(), dst_t.data_ptr(), len(pages),
                   self.pool.arena.data_ptr(), self.pool.nbytes, self.heads, self.dim, self.group,
-                  _lib.status_ptr(dev), _lib.stream_of(dev))
+                  _lib.SEM_PAGE, _lib.status_ptr(dev), _lib.stream_of(dev))
         for page, d in zip(pages, src):
             old_bits = {1: 4, 2: 8, 3: 16}[d & 3]
             self.pool.free(old_bits, d >> 8)  # stream order: later writes follow the repack
@@ -267,7 +267,7 @@ class PagedLayer:
         k = torch.empty((self.heads, n * BLOCK, self.dim), dtype=torch.float16, device=self.device)
         v = torch.empty_like(k)
         _lib.call("akv_unpack_pages", desc.data_ptr(), n, self.pool.arena.data_ptr(), self.pool.nbytes,
-                  self.heads, self.dim, self.group, k.data_ptr(), v.data_ptr(),
+                  self.heads, self.dim, self.group, k.data_ptr(), v.data_ptr(), _lib.DTYPE_F16,
                   _lib.status_ptr(self.device), _lib.stream_of(self.device))
         return k[:, :self.length].unsqueeze(0), v[:, :self.length].unsqueeze(0)
 

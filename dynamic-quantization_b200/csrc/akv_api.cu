@@ -15,7 +15,9 @@ extern "C" const char *akv_status_string(int status) {
 }
 
 // 3: V payloads stored in the bank-swizzled byte order (records of version 2 read differently).
-// 4: exchange buffers hold both epoch parities (akv_exchange_bytes doubled).
+// 4: exchange buffers hold both epoch parities (akv_exchange_bytes doubled);
+//    akv_repack_pages takes the quantizer semantics, akv_unpack_pages the output dtype;
+//    status words may live in mapped pinned host memory (akv_status_alloc).
 extern "C" int akv_abi_version(void) { return 4; }
 
 // The status word in mapped pinned host memory: kernels write it through the

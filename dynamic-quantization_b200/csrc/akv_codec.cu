@@ -9,6 +9,7 @@
 // the slab in registers, reduce the group absmax with warp shuffles and write
 // coalesced payload words.
 #include <algorithm>
+#include <type_traits>
 
 #include "akv_common.cuh"
 
@@ -130,6 +131,42 @@ __device__ __forceinline__ uint4 record_load8(int mode, const uint8_t *payload, 
     h[i] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
   }
   return make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+// The same 8 elements as float values int * float(scale), before any rounding
+// to fp16 (PackedTensor.dequantize, backend.py:177-180, rounds once to the
+// caller's dtype).  FP16 pages give their stored values.
+template <int D, int G, bool VPAY>
+__device__ __forceinline__ void record_load8_f32(int mode, const uint8_t *payload, const __half *sc, int c,
+                                                 int lane, float (&x)[8]) {
+  const int e = 256 * c + 8 * lane;
+  const int vx = VPAY ? v_chunk_xor<D>(mode, c, lane) : 0;
+  if (mode == AKV_MODE_FP16) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(payload + ((2 * e) ^ vx));
+    const uint32_t h[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = __half2float(__ushort_as_half((unsigned short)(h[i] & 0xffff)));
+      x[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(h[i] >> 16)));
+    }
+    return;
+  }
+  const float s = __half2float(sc[e / G]);
+  if (mode == AKV_MODE_INT8) {
+    const uint2 w = *reinterpret_cast<const uint2 *>(payload + (e ^ vx));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[i] = (float)(int)(int8_t)(w.x >> (8 * i)) * s;
+      x[4 + i] = (float)(int)(int8_t)(w.y >> (8 * i)) * s;
+    }
+  } else {
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(payload + ((e / 2) ^ vx));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int n = (w >> (4 * i)) & 15;
+      x[i] = (float)(n >= 8 ? n - 16 : n) * s;
+    }
+  }
 }
 
 // ---- exact quantization of a page slab without a division per element
@@ -351,13 +388,17 @@ __global__ void __launch_bounds__(256, SRC_RECORD ? 2 : 3) pack_pages_kernel(
   }
 }
 
-template <int D, int G>
+// Dequantize records to dense [heads][n_pages * 16][D] in OutT: fp16 gives
+// fp16(int * float(scale)) (QuantizedPage.dense, packed_decode.py:34-45);
+// fp32 / bf16 round int * float(scale) once to that type
+// (PackedTensor.dequantize, backend.py:177-180).
+template <int D, int G, typename OutT>
 __global__ void __launch_bounds__(256) unpack_pages_kernel(const int64_t *__restrict__ desc,
                                                            int64_t n_pages,
                                                            const uint8_t *__restrict__ arena,
                                                            int64_t arena_bytes, int heads,
-                                                           __half *__restrict__ out_k,
-                                                           __half *__restrict__ out_v,
+                                                           OutT *__restrict__ out_k,
+                                                           OutT *__restrict__ out_v,
                                                            int32_t *status) {
   constexpr int NC = Slab<D>::kChunks;
   const int lane = threadIdx.x & 31;
@@ -368,7 +409,7 @@ __global__ void __launch_bounds__(256) unpack_pages_kernel(const int64_t *__rest
     const int kv = (int)(it & 1);
     const int h = (int)((it >> 1) % heads);
     const int64_t p = (it >> 1) / heads;
-    __half *out = (kv ? out_v : out_k) + ((int64_t)h * n_pages + p) * kBlock * D;
+    OutT *out = (kv ? out_v : out_k) + ((int64_t)h * n_pages + p) * kBlock * D;
     const int64_t d = desc[p];
     const int mode = desc_mode(d);
     const int64_t rb = record_bytes(D, G, mode);
@@ -376,15 +417,29 @@ __global__ void __launch_bounds__(256) unpack_pages_kernel(const int64_t *__rest
     if (mode != AKV_MODE_SKIP && !ok && lane == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (ok) {
-        const uint8_t *rec = arena + desc_offset(d) + h * rb;
-        const int64_t pb = payload_bytes(D, mode);
-        const __half *sc = reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, mode);
-        v = kv ? record_load8<D, G, true>(mode, rec + pb, sc, c, lane)
-               : record_load8<D, G, false>(mode, rec, sc, c, lane);
+      OutT *dst = out + 256 * c + 8 * lane;
+      if constexpr (sizeof(OutT) == 2 && !std::is_same<OutT, __nv_bfloat16>::value) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (ok) {
+          const uint8_t *rec = arena + desc_offset(d) + h * rb;
+          const int64_t pb = payload_bytes(D, mode);
+          const __half *sc = reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, mode);
+          v = kv ? record_load8<D, G, true>(mode, rec + pb, sc, c, lane)
+                 : record_load8<D, G, false>(mode, rec, sc, c, lane);
+        }
+        *reinterpret_cast<uint4 *>(dst) = v;
+      } else {
+        float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (ok) {
+          const uint8_t *rec = arena + desc_offset(d) + h * rb;
+          const int64_t pb = payload_bytes(D, mode);
+          const __half *sc = reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, mode);
+          if (kv) record_load8_f32<D, G, true>(mode, rec + pb, sc, c, lane, x);
+          else record_load8_f32<D, G, false>(mode, rec, sc, c, lane, x);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = from_f32<OutT>(x[i]);
       }
-      *reinterpret_cast<uint4 *>(out + 256 * c + 8 * lane) = v;
     }
   }
 }
@@ -454,16 +509,23 @@ struct UnpackArgs {
   int64_t arena_bytes;
   int heads;
   void *out_k, *out_v;
+  int out_dtype;
   int32_t *status;
   cudaStream_t stream;
 };
 
 template <int D, int G>
 struct UnpackLaunch {
+  template <typename OutT>
+  static void go(const UnpackArgs &a) {
+    unpack_pages_kernel<D, G, OutT><<<grid_for(a.n_pages * a.heads * 2), 256, 0, a.stream>>>(
+        a.desc, a.n_pages, (const uint8_t *)a.arena, a.arena_bytes, a.heads, (OutT *)a.out_k,
+        (OutT *)a.out_v, a.status);
+  }
   static int run(const UnpackArgs &a) {
-    unpack_pages_kernel<D, G><<<grid_for(a.n_pages * a.heads * 2), 256, 0, a.stream>>>(
-        a.desc, a.n_pages, (const uint8_t *)a.arena, a.arena_bytes, a.heads, (__half *)a.out_k,
-        (__half *)a.out_v, a.status);
+    if (a.out_dtype == AKV_DTYPE_F16) go<__half>(a);
+    else if (a.out_dtype == AKV_DTYPE_F32) go<float>(a);
+    else go<__nv_bfloat16>(a);
     return launch_status();
   }
 };
@@ -551,24 +613,28 @@ extern "C" int akv_pack_pages(const void *src_k, const void *src_v, int64_t oute
 
 extern "C" int akv_repack_pages(const int64_t *src_desc, const int64_t *dst_desc, int64_t n_pages,
                                 void *arena, int64_t arena_bytes, int heads, int head_dim, int group,
-                                int32_t *dev_status, void *stream) {
+                                int semantics, int32_t *dev_status, void *stream) {
   if (int st = check_page_geometry(heads, head_dim, group)) return st;
   if (!src_desc || !dst_desc || !arena || n_pages < 0 || !aligned16(arena)) return AKV_ERR_INVALID;
+  if (semantics != AKV_SEM_TENSOR && semantics != AKV_SEM_PAGE) return AKV_ERR_INVALID;
   if (n_pages == 0) return AKV_OK;
   PackArgs a{nullptr, nullptr, 0, 0, 1, src_desc, dst_desc, n_pages, arena, arena_bytes, heads,
-             AKV_SEM_PAGE, dev_status, (cudaStream_t)stream};
+             semantics, dev_status, (cudaStream_t)stream};
   return head_dim == 64 ? dispatch_group<64, PackLaunch>(group, a, true)
                         : dispatch_group<128, PackLaunch>(group, a, true);
 }
 
 extern "C" int akv_unpack_pages(const int64_t *desc, int64_t n_pages, const void *arena,
                                 int64_t arena_bytes, int heads, int head_dim, int group, void *out_k,
-                                void *out_v, int32_t *dev_status, void *stream) {
+                                void *out_v, int out_dtype, int32_t *dev_status, void *stream) {
   if (int st = check_page_geometry(heads, head_dim, group)) return st;
   if (!desc || !arena || !out_k || !out_v || n_pages < 0) return AKV_ERR_INVALID;
   if (!aligned16(arena) || !aligned16(out_k) || !aligned16(out_v)) return AKV_ERR_INVALID;
+  if (out_dtype != AKV_DTYPE_F16 && out_dtype != AKV_DTYPE_F32 && out_dtype != AKV_DTYPE_BF16)
+    return AKV_ERR_INVALID;
   if (n_pages == 0) return AKV_OK;
-  UnpackArgs a{desc, n_pages, arena, arena_bytes, heads, out_k, out_v, dev_status, (cudaStream_t)stream};
+  UnpackArgs a{desc, n_pages, arena, arena_bytes, heads, out_k, out_v, out_dtype, dev_status,
+               (cudaStream_t)stream};
   return head_dim == 64 ? dispatch_group<64, UnpackLaunch>(group, a)
                         : dispatch_group<128, UnpackLaunch>(group, a);
 }

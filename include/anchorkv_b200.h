@@ -119,18 +119,25 @@ int akv_pack_pages(const void *src_k, const void *src_v, int64_t outer_stride,
                    int head_dim, int group, int semantics, int32_t *dev_status, void *stream);
 
 /* Requantize pages in the arena: dequantize src records to fp16 exactly as
- * QuantizedPage.dense does, then pack with pack_page semantics into dst records.
- * Replaces PagedLayer.demote (packed_decode.py:164-174). Source and
- * destination records must not overlap. */
+ * QuantizedPage.dense does (fp16(int * float(scale)); FP16 records as stored),
+ * then pack into dst records with `semantics`: AKV_SEM_PAGE (pack_page) or
+ * AKV_SEM_TENSOR (quantize_tensor on fp16 values).  Source and destination
+ * records must not overlap.  Replaces PagedLayer.demote (packed_decode.py:164-174)
+ * and the per-block dequantize + quantize_tensor loop of
+ * DeclarativeKVCache.requantize_segment (backend.py:470-483). */
 int akv_repack_pages(const int64_t *src_desc, const int64_t *dst_desc, int64_t n_pages,
                      void *arena, int64_t arena_bytes, int heads, int head_dim, int group,
-                     int32_t *dev_status, void *stream);
+                     int semantics, int32_t *dev_status, void *stream);
 
-/* Dequantize pages to dense fp16 out_k/out_v[heads][n_pages*16][head_dim]
- * (skipped pages read as zeros).  Replaces PagedLayer.dense (packed_decode.py:189-194). */
+/* Dequantize pages to dense out_k/out_v[heads][n_pages*16][head_dim] of
+ * out_dtype (skipped pages read as zeros): AKV_DTYPE_F16 gives
+ * fp16(int * float(scale)) as QuantizedPage.dense; AKV_DTYPE_F32 / _BF16 round
+ * int * float(scale) once to that type, as PackedTensor.dequantize does.
+ * Replaces PagedLayer.dense (packed_decode.py:189-194) and the block
+ * dequantisation of DeclarativeKVCache.materialize_segments (backend.py:557-591). */
 int akv_unpack_pages(const int64_t *desc, int64_t n_pages, const void *arena,
                      int64_t arena_bytes, int heads, int head_dim, int group, void *out_k,
-                     void *out_v, int32_t *dev_status, void *stream);
+                     void *out_v, int out_dtype, int32_t *dev_status, void *stream);
 
 /* Bytes of the workspace akv_decode_partials / akv_packed_attention need for
  * this geometry on the current device (-1 for invalid or unsupported arguments).

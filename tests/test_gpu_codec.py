@@ -116,11 +116,12 @@ def test_repack_and_unpack_match_page_semantics(cuda, dim, src_bits, dst_bits):
     dst_desc = torch.tensor([P.encode(dst_bits, 16, int(o)) for o in offs], dtype=torch.int64, device=cuda)
     from anchorkv_b200 import _lib
     _lib.call("akv_repack_pages", src.table.data_ptr(), dst_desc.data_ptr(), n, pool.arena.data_ptr(),
-              pool.nbytes, heads, dim, group, _lib.status_word(cuda).data_ptr(), _lib.stream_of(cuda))
+              pool.nbytes, heads, dim, group, _lib.SEM_PAGE, _lib.status_word(cuda).data_ptr(), _lib.stream_of(cuda))
     ok = torch.empty((heads, n * 16, dim), dtype=torch.float16, device=cuda)
     ov = torch.empty_like(ok)
     _lib.call("akv_unpack_pages", dst_desc.data_ptr(), n, pool.arena.data_ptr(), pool.nbytes, heads, dim,
-              group, ok.data_ptr(), ov.data_ptr(), _lib.status_word(cuda).data_ptr(), _lib.stream_of(cuda))
+              group, ok.data_ptr(), ov.data_ptr(), _lib.DTYPE_F16, _lib.status_word(cuda).data_ptr(),
+              _lib.stream_of(cuda))
     assert akv.take_device_status(cuda) == 0
     for t, got in ((k, ok), (v, ov)):
         for j in range(n):

@@ -62,7 +62,8 @@ def _dense(store, b0, b1):
     k = torch.empty((heads, n * 16, D), dtype=torch.float16, device=dev)
     v = torch.empty_like(k)
     _lib.call("akv_unpack_pages", desc.data_ptr(), n, store.pool.arena.data_ptr(), store.pool.nbytes, heads, D,
-              store.group, k.data_ptr(), v.data_ptr(), _lib.status_word(dev).data_ptr(), _lib.stream_of(dev))
+              store.group, k.data_ptr(), v.data_ptr(), _lib.DTYPE_F16, _lib.status_word(dev).data_ptr(),
+              _lib.stream_of(dev))
     keep = ((desc & 3) != 0).view(b1 - b0, -1).repeat_interleave(16, dim=1)
     return k.view(heads, b1 - b0, -1, D).transpose(0, 1), v.view(heads, b1 - b0, -1, D).transpose(0, 1), keep
 
