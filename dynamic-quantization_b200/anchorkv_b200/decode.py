@@ -54,15 +54,28 @@ def _store_geometry(layer):
     return layer.pool.arena, layer.pool.nbytes, layer.table.view(1, -1), None, n
 
 
+def _as_table(layer):
+    """A DeclarativeKVCache stands for its (single) layer's visible page table."""
+    if hasattr(layer, "decode_view"):
+        if layer.layers > 1:
+            raise ValueError("the store holds several layers: pass store.decode_view(layer)")
+        return layer.decode_view(0)
+    return layer
+
+
 def packed_attention(query, layer, scale, splits=4, *, out=None):
     """Attend one query token per sequence over the layer's packed pages.
 
+    ``layer``: a PagedLayer, a PagedBatch, or a DeclarativeKVCache of one layer
+    (its visible, non-evicted blocks; ``store.decode_view(l)`` for layer l of a
+    multi-layer store).
     ``query``: fp16 CUDA ``[batch, Hq, 1, D]`` (batch 1 for a PagedLayer).
     ``splits``: at least this many pieces per (sequence, KV head), merged by
     LSE (the reference's split-K knob); the decode cuts finer, down to 16 pages
     a piece, while the device has resident warps to spare (``0``: every
     resident warp).  Results do not depend on it beyond fp32 rounding.
     """
+    layer = _as_table(layer)
     batched = isinstance(layer, PagedBatch)
     batch = layer.batch if batched else 1
     if query.shape[0] != batch or query.shape[2] != 1 or query.shape[-1] != layer.dim:
@@ -104,6 +117,7 @@ def decode_partial_states(query, layer, scale, splits=0):
     Returns fp32 ``[batch, Hq, D + 2]`` = (acc[D], m, l) with ``m`` in base-2
     units of the scaled score, for a further merge (e.g. across GPUs holding
     contiguous shards of each sequence) with :func:`merge_states`."""
+    layer = _as_table(layer)
     batched = isinstance(layer, PagedBatch)
     batch = layer.batch if batched else 1
     heads = query.shape[1]

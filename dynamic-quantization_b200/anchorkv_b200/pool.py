@@ -157,6 +157,31 @@ class PagePool:
     def free(self, bits: int, offset: int) -> None:
         self._free[bits].append(int(offset))
 
+    def free_many(self, bits: int, offsets) -> None:
+        self._free[bits].extend(int(o) for o in np.asarray(offsets).reshape(-1))
+
+    def reserve(self, bits: int, n: int) -> None:
+        """Make at least ``n`` slots of ``bits`` free, growing the arena if needed.
+
+        Growth appends a region of new slots (at least doubling the class) and
+        copies the old arena into a larger one on the current stream: byte
+        offsets, and so descriptors, stay valid, but tensors viewing the old
+        arena (``page_view``) do not follow.  Owners that hand out page views
+        (``PagedLayer``) never grow their pool."""
+        short = n - len(self._free[bits])
+        if short <= 0:
+            return
+        extra = max(short, self.capacity[bits], 64)
+        start = self.nbytes
+        old = self.arena
+        self.nbytes = start + extra * self.page_bytes[bits]
+        self.arena = torch.empty(self.nbytes, dtype=torch.uint8, device=self.device)
+        self.arena[:start].copy_(old[:start])
+        self.arena[start:].zero_()
+        new = start + np.arange(extra, dtype=np.int64) * self.page_bytes[bits]
+        self._free[bits] = list(new[::-1]) + self._free[bits]  # old free slots are taken first
+        self.capacity[bits] += extra
+
     def page_view(self, offset: int, bits: int) -> torch.Tensor:
         """uint8 view ``[heads, record_bytes]`` of one page."""
         rec = self.page_bytes[bits] // self.heads
@@ -176,6 +201,15 @@ class PagedBatch:
         self.batch, self.max_blocks = batch, max_blocks
         self.table = torch.zeros((batch, max_blocks), dtype=torch.int64, device=pool.device)
         self.seq_blocks = torch.full((batch,), max_blocks, dtype=torch.int32, device=pool.device)
+
+    @classmethod
+    def over(cls, pool: PagePool, table: torch.Tensor) -> "PagedBatch":
+        """A batch over an existing ``[batch, max_blocks]`` descriptor table (a
+        view, no allocation); every sequence uses all ``max_blocks`` entries."""
+        view = cls.__new__(cls)
+        view.pool, view.table, view.seq_blocks = pool, table, None
+        view.batch, view.max_blocks = int(table.shape[0]), int(table.shape[1])
+        return view
 
     heads = property(lambda self: self.pool.heads)
     dim = property(lambda self: self.pool.dim)

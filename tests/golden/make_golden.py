@@ -13,7 +13,10 @@ report on seeded inputs, and writes:
 * ``codec.npz`` + ``codec.json`` -- quantizer inputs, payloads, scales, dequantised values;
 * ``attention.npz`` + ``attention.json`` -- decode outputs and sha256 digests of
   the dense K/V the reference attended over;
-* ``demo.json`` -- the ``requantize-demo`` storage report (INT4 and INT8).
+* ``demo.json`` -- the ``requantize-demo`` storage report (INT4 and INT8);
+* ``declarative.npz`` + ``declarative.json`` -- the block store on page-format
+  scenarios: visibility, positions, storage reports, digests of the dense K/V
+  and per-layer decode outputs.
 
 Nothing at test time reads the reference; the tests read these files.
 """
@@ -230,6 +233,54 @@ def build_attention(anchorkv):
     (HERE / "attention.json").write_text(json.dumps(meta, indent=1))
 
 
+def build_declarative(anchorkv):
+    """The reference's DeclarativeKVCache on the page-format scenarios of
+    workloads.DECLARATIVE: per recorded view the visible segments, positions,
+    the storage report, sha256 digests of the dense K/V it materialises (in the
+    original fp16 and as fp32 / bf16) and the SDPA output of every layer over
+    the visible fp16 K/V."""
+    from anchorkv.backend import DeclarativeKVCache, SegmentRole
+    from anchorkv.policy import CacheMode
+
+    arrays, meta = {}, []
+    for spec in W.DECLARATIVE:
+        kv, queries = W.declarative_inputs(spec)
+        cache = DeclarativeKVCache(block_size=16, group_size=spec["group"])
+        for sid, start, _, role in spec["segments"]:
+            cache.add_segment(sid, kv[sid][0], kv[sid][1], token_start=start, role=SegmentRole(role))
+        for step in spec["steps"]:
+            if step[0] == "feed":
+                cache.feed_declarations(step[1])
+            else:
+                cache.requantize_segment(step[1], CacheMode(step[2]))
+        record = {"name": spec["name"], "inputs_sha": W.sha256(*[t for sid in sorted(kv) for t in kv[sid]],
+                                                                 *queries), "views": []}
+        for i, view in enumerate(spec["views"]):
+            cache.feed_declarations(view)
+            mat = cache.materialize_visible()
+            f32 = cache.materialize_visible(dtype=torch.float32)
+            b16 = cache.materialize_visible(dtype=torch.bfloat16)
+            key5 = mat.key if mat.key.ndim == 5 else mat.key[None]
+            val5 = mat.value if mat.value.ndim == 5 else mat.value[None]
+            outs = []
+            for layer, q in enumerate(queries):
+                g = spec["q_heads"] // key5.shape[2]
+                outs.append(F.scaled_dot_product_attention(
+                    q, key5[layer].repeat_interleave(g, 1), val5[layer].repeat_interleave(g, 1),
+                    scale=1.0 / math.sqrt(spec["dim"])))
+            out_key = f"decl_{spec['name']}_{i}"
+            arrays[out_key] = _np(torch.stack(outs))
+            record["views"].append({
+                "directive": view, "visible": list(cache.visible_segment_ids()),
+                "positions": mat.positions.tolist(), "block_ids": list(mat.block_ids),
+                "segment_ids": list(mat.segment_ids), "dense_sha_f16": W.sha256(mat.key, mat.value),
+                "dense_sha_f32": W.sha256(f32.key, f32.value), "dense_sha_bf16": W.sha256(b16.key, b16.value),
+                "shape": list(mat.key.shape), "report": cache.storage_report(), "out": out_key})
+        meta.append(record)
+    np.savez_compressed(HERE / "declarative.npz", **arrays)
+    (HERE / "declarative.json").write_text(json.dumps(meta, indent=1))
+
+
 def build_demo(anchorkv):
     from anchorkv.cli import run_requantization_demo
     from anchorkv.policy import CacheMode
@@ -239,7 +290,9 @@ def build_demo(anchorkv):
 
 
 def main():
-    src = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <reference source dir holding anchorkv/>")
+    src = Path(sys.argv[1])
     sys.path.insert(0, str(src))
     import anchorkv
 
@@ -247,6 +300,7 @@ def main():
     build_codec(anchorkv)
     build_attention(anchorkv)
     build_demo(anchorkv)
+    build_declarative(anchorkv)
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".npz", ".json")))
 
 

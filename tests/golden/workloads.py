@@ -102,3 +102,46 @@ GATE_BITS = (4, 8, 16)
 
 def gate_seed(dim: int, length: int, bits: int) -> int:
     return 1000 * dim + 10 * length + bits
+
+
+# Declarative-store scenarios in the decode page format (fp16 K/V, 16-token
+# blocks).  Each segment is (segment id, token start, tokens, role); ``steps``
+# run in order, then each of ``views`` (directive text fed to the store) gives
+# one recorded state.  "mixed" holds one segment whose partial block a scale
+# group would straddle (37 tokens x head_dim 64, group 128), which cannot be a
+# page record and stays flat.
+DECLARATIVE = [
+    dict(name="slab_4d", lead=(1, 8), dim=128, group=2048, q_heads=16, seed=501,
+         segments=[(0, 0, 16, "sink"), (1, 16, 32, "scaffold"), (2, 48, 64, "context"), (3, 112, 48, "context"),
+                   (4, 176, 80, "context"), (5, 256, 32, "response")],
+         steps=[("requantize", 2, "int8"), ("requantize", 2, "int4"), ("requantize", 3, "int4"),
+                ("requantize", 4, "int8"), ("feed", '<anchor segments="0">'), ("requantize", 1, "evicted")],
+         views=["", '<focus segments="3">', "<local>", "</local>"]),
+    dict(name="rows_5d", lead=(2, 3, 4), dim=64, group=64, q_heads=8, seed=777,
+         segments=[(0, 0, 37, "sink"), (1, 40, 21, "context"), (2, 61, 16, "context"), (3, 90, 45, "context"),
+                   (4, 135, 9, "response")],
+         steps=[("requantize", 1, "int8"), ("requantize", 1, "int4"), ("requantize", 3, "int8"),
+                ("feed", '<archive segments="2">'), ("requantize", 0, "int8")],
+         views=["", '<focus segments="1,3">', "<local>"]),
+    dict(name="rows_g32_d128", lead=(2, 4), dim=128, group=32, q_heads=8, seed=913,
+         segments=[(0, 0, 33, "scaffold"), (1, 33, 50, "context"), (2, 83, 7, "response")],
+         steps=[("requantize", 1, "int4"), ("requantize", 0, "int8")],
+         views=["", "<local>"]),
+    dict(name="mixed", lead=(2, 4), dim=64, group=128, q_heads=8, seed=1201,
+         segments=[(0, 0, 32, "sink"), (1, 32, 37, "context"), (2, 69, 48, "response")],
+         steps=[("requantize", 1, "int8"), ("requantize", 2, "int4")],
+         views=["", "<local>"]),
+]
+
+
+def declarative_inputs(spec):
+    """K/V per segment (fp16, ``lead + (tokens, dim)``) and one query per layer
+    (``[batch, q_heads, 1, dim]``)."""
+    kv = {}
+    for sid, _, tokens, _ in spec["segments"]:
+        shape = tuple(spec["lead"]) + (tokens, spec["dim"])
+        kv[sid] = (outlier_kv(spec["seed"] + 10 * sid, shape), outlier_kv(spec["seed"] + 10 * sid + 1, shape))
+    lead = tuple(spec["lead"])
+    layers, batch = (lead[0], lead[1]) if len(lead) == 3 else (1, lead[0])
+    q = [normal(spec["seed"] + 1000 + layer, (batch, spec["q_heads"], 1, spec["dim"])) for layer in range(layers)]
+    return kv, q

@@ -149,7 +149,7 @@ def cpu_cache(monkeypatch):
 
 def test_block_store_lifecycle_rules(cpu_cache):
     c = cpu_cache
-    assert [len(c._segment_blocks[s]) for s in range(4)] == [1, 2, 2, 1]
+    assert [s["blocks"] for s in c.storage_report()["segments"]] == [1, 2, 2, 1]
     with pytest.raises(ValueError, match="overlap"):
         c.add_segment(9, torch.randn(1, 2, 3, 8), torch.randn(1, 2, 3, 8), token_start=2)
     with pytest.raises(ValueError, match="already registered"):
