@@ -40,6 +40,9 @@ PROTOTYPES = {
                                         ctypes.c_int, ctypes.c_int, _c_p, _c_p]),
     "akv_unpack_pages": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_int, _c_p, _c_p, ctypes.c_int, _c_p, _c_p]),
+    "akv_append_rows": (ctypes.c_int, [_c_p, _c_p, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       _c_p, _i64, ctypes.c_int, _c_p, _c_p, _i64, ctypes.c_int, ctypes.c_int,
+                                       _c_p, _c_p]),
     "akv_workspace_bytes": (_i64, [ctypes.c_int] * 6),
     "akv_decode_partials": (ctypes.c_int, [_c_p, _i64, _c_p, _i64, _c_p, _i32, _c_p, _i64, _i64,
                                            _i32, _i32, _i32, _i32, _i32, _f32, _i32, _c_p, _i64, _c_p,

@@ -1,15 +1,31 @@
-"""Hugging Face decode loops over the packed store: the paged layers as a live
-cache and the packed kernel as the model's attention.
+"""Batched Hugging Face decode over the packed store.
 
-Mirrors the reference's model-side integration in
-``src/anchorkv/colab_experiment.py``: ``stock_cache`` / ``cache_cpu`` (:86-91),
-``make_live_cache`` (:92-120), ``attention_route`` (:123-148) and
-``forward_token`` (:150-155), the decode loop of ``run_policy`` (:191-214) and
-``model_gate`` (:294-313), whose acceptance rule is the parity check here: over
-the same stores, the packed route's logits stay within a mean per-token KL of
-0.002 of the dense route's, and the FP16 paged route matches the stock model.
-``controlled_decode`` is the reference's fixed-history timing harness
-(``src/anchorkv/benchmark_suite.py:155-264``).
+The reference decodes one sequence at a time: its ``LiveCache`` holds one
+``PagedLayer`` per layer and its attention route calls the packed kernel per
+layer (``src/anchorkv/colab_experiment.py:92-148``).  That route runs
+unchanged on this package: its ``PagedLayer``, ``dense_attention`` and
+``packed_attention`` are drop-ins (see the integration notes), and the tests
+run the reference's own route, model gate and controlled-decode harness
+(``src/anchorkv/benchmark_suite.py:155-264``) with them substituted.
+
+What is new here is a batch: :class:`PagedKVStore` keeps the pages of
+``batch`` sequences for every layer in one shared :class:`PagePool`, one page
+table per layer that :func:`packed_attention` reads as a ``PagedBatch``:
+
+* prefill packs every layer's prefix in one ``akv_pack_pages`` launch, pages
+  older than the recent window straight to the archive precision (pack_page
+  rounding, the same bytes the reference's append-then-demote gives);
+* a decode step appends each layer's new K/V rows for all sequences in one
+  ``akv_append_rows`` launch, which also advances the pages' valid-token
+  counts on the device; a fresh page's descriptors reach the table through
+  the same launch (one pinned, non-blocking copy of ``batch`` descriptors);
+* when a page leaves the recent window it is demoted for all sequences at
+  once (``akv_repack_pages``) and its FP16 slots return to the pool.
+
+:func:`batched_live_cache` wraps the store as a transformers ``DynamicCache``
+and :func:`paged_route` registers an attention function that decodes through
+it, so a batched ``model(...)`` step runs two kernel launches per layer for
+attention (decode, merge) plus one append.
 
 Model code (``transformers``) is imported lazily: it is needed only when a
 model runs.
@@ -18,268 +34,282 @@ model runs.
 from __future__ import annotations
 
 from contextlib import contextmanager
-from dataclasses import dataclass
 
+import numpy as np
 import torch
 
+from . import _lib
+from . import pool as P
 from .decode import packed_attention
-from .packed_decode import PagedLayer, dense_attention, kl_divergence
 
-# Name the routed attention function is registered under.
-ROUTE = "anchorkv_b200"
-
-
-@dataclass
-class Settings:
-    """The fields of the reference's experiment settings (colab_experiment.py:21-35)
-    that the live cache and the decode loop read."""
-
-    block: int = 16
-    recent_pages: int = 2
-    max_new_tokens: int = 48
+# Name the batched attention function is registered under.
+ROUTE = "anchorkv_b200_batched"
 
 
-def stock_cache(source, device="cuda"):
-    """A stock ``DynamicCache`` holding ``source`` = [(key, value)] per layer."""
-    from transformers import DynamicCache
+class PagedKVStore:
+    """Pages of ``batch`` sequences for ``layers`` layers over one shared pool.
 
-    return DynamicCache([(k.to(device), v.to(device)) for k, v in source])
+    Sequences of a batch advance together (one decode token each per step).
+    Pages start FP16; a complete page older than the ``recent_pages`` most
+    recent ones is demoted to ``archive_bits`` unless its index is in
+    ``protected`` (the lifecycle of the reference's PagedLayer,
+    packed_decode.py:135-179, for every sequence at once)."""
+
+    def __init__(self, layers: int, batch: int, heads: int, dim: int, max_tokens: int, *, group: int = 64,
+                 archive_bits: int = 4, recent_pages: int = 2, protected=(), device="cuda"):
+        if archive_bits not in (4, 8, 16):
+            raise ValueError("archive_bits must be 4, 8 or 16")
+        if dim not in (64, 128) or not P.group_ok(dim, group) or group > dim:
+            raise ValueError("supported geometry: head dim 64/128, group 32/64/128 dividing it")
+        self.layers, self.batch, self.heads, self.dim, self.group = layers, batch, heads, dim, group
+        self.archive_bits, self.recent_pages = archive_bits, recent_pages
+        self.protected = frozenset(int(p) for p in protected)
+        self.device = torch.device(device)
+        self.capacity = -(-max_tokens // P.BLOCK)
+        hot = self.capacity if archive_bits == 16 else min(self.capacity, recent_pages + 2 + len(self.protected))
+        sizes = {16: layers * batch * hot}
+        if archive_bits != 16:
+            sizes[archive_bits] = layers * batch * self.capacity
+        self.pool = P.PagePool(heads, dim, group=group, pages=sizes, device=self.device, zero=False)
+        self.tables = torch.zeros((layers, batch, self.capacity), dtype=torch.int64, device=self.device)
+        self._desc = np.zeros((layers, batch, self.capacity), np.int64)  # host mirror of the tables
+        self.lengths = [0] * layers
+        self._archived = [-1] * layers
+        self.demotions = 0
+
+    # ------------------------------------------------------------- writes
+    def prefill(self, layer: int, key: torch.Tensor, value: torch.Tensor) -> None:
+        """Store a prefix ``[batch, heads, tokens, dim]`` of an empty layer."""
+        if self.lengths[layer]:
+            raise ValueError("prefill needs an empty layer; decode steps go through append")
+        batch, heads, tokens, dim = key.shape
+        if (batch, heads, dim) != (self.batch, self.heads, self.dim) or value.shape != key.shape:
+            raise ValueError("key/value geometry does not match the store")
+        if tokens > self.capacity * P.BLOCK:
+            raise ValueError("cache geometry or capacity exceeded")
+        _lib.require_cuda(key, "key")
+        n = -(-tokens // P.BLOCK)
+        eligible = tokens // P.BLOCK - self.recent_pages  # complete pages older than the recent window
+        bits = np.full(n, 16)
+        if self.archive_bits != 16:
+            old = np.arange(n) < eligible
+            old[list(p for p in self.protected if p < n)] = False
+            bits[old] = self.archive_bits
+        ntok = np.minimum(P.BLOCK, tokens - P.BLOCK * np.arange(n))
+        desc = np.zeros((batch, n), np.int64)
+        for b_ in (16, 8, 4):
+            cols = np.nonzero(bits == b_)[0]
+            if cols.size:
+                self.pool.reserve(b_, batch * cols.size)
+                offs = self.pool.alloc_many(b_, batch * cols.size).reshape(batch, cols.size)
+                desc[:, cols] = P.encode_array(np.full(offs.shape, P.BITS_TO_MODE[b_]),
+                                               np.broadcast_to(ntok[cols], offs.shape), offs)
+        pad = n * P.BLOCK - tokens
+        k = torch.nn.functional.pad(key.half(), (0, 0, 0, pad)).contiguous()
+        v = torch.nn.functional.pad(value.half(), (0, 0, 0, pad)).contiguous()
+        d = _to_device(desc.reshape(-1), self.device)
+        _lib.call("akv_pack_pages", k.data_ptr(), v.data_ptr(), heads * n * P.BLOCK * dim, n * P.BLOCK * dim, n,
+                  batch * n, d.data_ptr(), self.pool.arena.data_ptr(), self.pool.nbytes, heads, dim, self.group,
+                  _lib.SEM_PAGE, _lib.status_ptr(self.device), _lib.stream_of(self.device))
+        self.tables[layer, :, :n].copy_(d.view(batch, n))
+        self._desc[layer, :, :n] = desc
+        self.lengths[layer] = tokens
+        self._archived[layer] = max(eligible - 1, -1)
+
+    def append(self, layer: int, key: torch.Tensor, value: torch.Tensor) -> None:
+        """Append ``[batch, heads, rows, dim]`` decode-step K/V to every sequence."""
+        if key.shape != value.shape or key.shape[0] != self.batch or key.shape[1] != self.heads \
+                or key.shape[-1] != self.dim:
+            raise ValueError("key/value geometry does not match the store")
+        rows = key.shape[2]
+        if self.lengths[layer] + rows > self.capacity * P.BLOCK:
+            raise ValueError("cache geometry or capacity exceeded")
+        key, value = _halves(key), _halves(value)
+        status, stream = _lib.status_ptr(self.device), _lib.stream_of(self.device)
+        done = 0
+        while done < rows:
+            page, row = divmod(self.lengths[layer], P.BLOCK)
+            take = min(P.BLOCK - row, rows - done)
+            fresh = None
+            if row == 0:  # a new FP16 page for every sequence
+                self.pool.reserve(16, self.batch)
+                offs = self.pool.alloc_many(16, self.batch)
+                new = P.encode_array(np.full(self.batch, _lib.MODE_FP16), np.full(self.batch, take), offs)
+                fresh = _to_device(new, self.device)
+                self._desc[layer, :, page] = new
+            else:
+                self._desc[layer, :, page] = (self._desc[layer, :, page] & ~np.int64(15 << 2)) | ((row + take - 1) << 2)
+            k, v = key[:, :, done:done + take], value[:, :, done:done + take]
+            tbl = self.tables[layer]
+            _lib.call("akv_append_rows", k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+                      self.batch, take, row, tbl.data_ptr(), tbl.stride(0), page,
+                      None if fresh is None else fresh.data_ptr(), self.pool.arena.data_ptr(), self.pool.nbytes,
+                      self.heads, self.dim, status, stream)
+            self.lengths[layer] += take
+            done += take
+            self._archive(layer)
+
+    def _archive(self, layer: int) -> None:
+        last = self.lengths[layer] // P.BLOCK - self.recent_pages - 1
+        pages = [p for p in range(self._archived[layer] + 1, last + 1) if p not in self.protected]
+        self._archived[layer] = max(self._archived[layer], last)
+        if self.archive_bits == 16 or not pages:
+            return
+        src = self._desc[layer][:, pages]  # [batch, n]
+        self.pool.reserve(self.archive_bits, src.size)
+        offs = self.pool.alloc_many(self.archive_bits, src.size)
+        dst = P.encode_array(np.full(src.shape, P.BITS_TO_MODE[self.archive_bits]), ((src >> 2) & 15) + 1,
+                             offs.reshape(src.shape))
+        s_dev, d_dev = _to_device(src.reshape(-1), self.device), _to_device(dst.reshape(-1), self.device)
+        _lib.call("akv_repack_pages", s_dev.data_ptr(), d_dev.data_ptr(), src.size, self.pool.arena.data_ptr(),
+                  self.pool.nbytes, self.heads, self.dim, self.group, _lib.SEM_PAGE, _lib.status_ptr(self.device),
+                  _lib.stream_of(self.device))
+        self.tables[layer][:, pages] = d_dev.view(src.shape)
+        self._desc[layer][:, pages] = dst
+        self.pool.free_many(16, src >> 8)  # stream order: later writes to these slots follow the repack
+        self.demotions += src.size
+
+    # -------------------------------------------------------------- reads
+    def pages(self, layer: int = 0) -> int:
+        return -(-self.lengths[layer] // P.BLOCK)
+
+    def batch_view(self, layer: int) -> P.PagedBatch:
+        """Layer ``layer``'s page table for :func:`packed_attention` (query ``[batch, Hq, 1, D]``)."""
+        return P.PagedBatch.over(self.pool, self.tables[layer, :, :self.pages(layer)])
+
+    def bits(self, layer: int = 0) -> np.ndarray:
+        """Precision of every page, ``[batch, pages]``."""
+        modes = self._desc[layer, :, :self.pages(layer)] & 3
+        return np.vectorize(P.MODE_TO_BITS.get)(modes)
+
+    @property
+    def payload_bytes(self) -> int:
+        """Payload + scale bytes of every page (QuantizedPage.nbytes of K and V, packed_decode.py:28-32)."""
+        total = 0
+        for layer in range(self.layers):
+            bits = self.bits(layer)
+            for b_ in (16, 8, 4):
+                per_page = self.heads * (2 * P.BLOCK * self.dim * b_ // 8 +
+                                         (0 if b_ == 16 else 4 * P.BLOCK * self.dim // self.group))
+                total += int((bits == b_).sum()) * per_page
+        return total
+
+    @property
+    def resident_bytes(self) -> int:
+        """Payload + scales + the page tables (8 bytes per page slot)."""
+        return self.payload_bytes + self.tables.numel() * 8
+
+    def dense(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """fp16 K, V ``[batch, heads, tokens, dim]`` as the pages hold them."""
+        n = self.pages(layer)
+        desc = self.tables[layer, :, :n].contiguous()
+        k = torch.empty((self.heads, self.batch * n * P.BLOCK, self.dim), dtype=torch.float16, device=self.device)
+        v = torch.empty_like(k)
+        _lib.call("akv_unpack_pages", desc.data_ptr(), self.batch * n, self.pool.arena.data_ptr(), self.pool.nbytes,
+                  self.heads, self.dim, self.group, k.data_ptr(), v.data_ptr(), _lib.DTYPE_F16,
+                  _lib.status_ptr(self.device), _lib.stream_of(self.device))
+        shape = (self.heads, self.batch, n * P.BLOCK, self.dim)
+        length = self.lengths[layer]
+        return (k.view(shape).transpose(0, 1)[:, :, :length], v.view(shape).transpose(0, 1)[:, :, :length])
+
+    def report(self) -> dict:
+        return {"resident_bytes": self.resident_bytes, "payload_bytes": self.payload_bytes,
+                "demotions": self.demotions, "tokens": self.lengths[0], "batch": self.batch}
 
 
-def cache_cpu(cache):
-    """[(key, value)] per layer of a stock cache, on the host."""
-    return [(layer.keys.detach().cpu(), layer.values.detach().cpu()) for layer in cache.layers]
+def _halves(t: torch.Tensor) -> torch.Tensor:
+    """fp16 with head_dim contiguous and 8-byte aligned rows (akv_append_rows' input)."""
+    t = t.to(torch.float16)
+    if t.stride(-1) != 1 or t.data_ptr() % 8 or any(s % 4 for s in t.stride()[:3]):
+        t = t.contiguous()
+    return t
 
 
-def make_live_cache(source, settings, protected=(), bits=4, max_tokens=None, device="cuda"):
-    """A ``DynamicCache`` whose layers are :class:`PagedLayer` stores: prefilled
-    from ``source``, appended to (and demoted to ``bits``) as tokens are decoded.
-    ``update`` hands the new keys/values back unchanged; the routed attention
-    reads the stores."""
-    from transformers import DynamicCache
+def _to_device(array: np.ndarray, device) -> torch.Tensor:
+    """An int64 host array on ``device`` through pinned memory, without blocking
+    the host (torch keeps the pinned block until the copy has run)."""
+    return torch.from_numpy(np.ascontiguousarray(array, np.int64)).pin_memory().to(device, non_blocking=True)
 
-    if max_tokens is None:
-        max_tokens = source[0][0].shape[-2] + settings.max_new_tokens + 32
 
-    class LiveCache(DynamicCache):
-        def __init__(self):
-            super().__init__()
-            self.stores = []
-            for key, value in source:
-                store = PagedLayer(key.shape[1], key.shape[-1], max_tokens, block=settings.block,
-                                   archive_bits=bits, protected=protected,
-                                   recent_pages=settings.recent_pages, device=device)
-                store.append(key.to(device), value.to(device))
-                self.stores.append(store)
+_CACHE_CLASS = None
 
-        def get_seq_length(self, layer_idx=0):
-            return self.stores[layer_idx].length
 
-        def update(self, key_states, value_states, layer_idx, *args, **kwargs):
-            self.stores[layer_idx].append(key_states, value_states)
-            return key_states, value_states
+def batched_live_cache(source, *, max_tokens: int, group: int = 64, archive_bits: int = 4, recent_pages: int = 2,
+                       protected=(), device="cuda"):
+    """A transformers ``DynamicCache`` over a :class:`PagedKVStore`, prefilled
+    from ``source`` = [(key, value)] per layer, each ``[batch, heads, tokens,
+    dim]`` (e.g. a stock cache's layers after a batched prefill).  ``update``
+    appends the step's keys/values to the store and hands them back unchanged;
+    the routed attention (:func:`paged_route`) reads the store."""
+    global _CACHE_CLASS
+    if _CACHE_CLASS is None:
+        from transformers import DynamicCache
 
-        def report(self):
-            return {"resident_bytes": sum(s.resident_bytes for s in self.stores),
-                    "payload_bytes": sum(s.payload_bytes for s in self.stores),
-                    "demotions": sum(s.demotions for s in self.stores),
-                    "tokens": self.get_seq_length()}
+        class BatchedLiveCache(DynamicCache):
+            def __init__(self, store: PagedKVStore):
+                super().__init__()
+                self.store = store
 
-    return LiveCache()
+            def get_seq_length(self, layer_idx=0):
+                return self.store.lengths[layer_idx]
+
+            def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
+                self.store.append(layer_idx, key_states, value_states)
+                return key_states, value_states
+
+            def report(self):
+                return self.store.report()
+
+        _CACHE_CLASS = BatchedLiveCache
+    key0 = source[0][0]
+    store = PagedKVStore(len(source), key0.shape[0], key0.shape[1], key0.shape[-1], max_tokens, group=group,
+                         archive_bits=archive_bits, recent_pages=recent_pages, protected=protected, device=device)
+    for layer, (key, value) in enumerate(source):
+        store.prefill(layer, key.to(device), value.to(device))
+    return _CACHE_CLASS(store)
 
 
 @contextmanager
-def attention_route(model, cache=None, backend="dense", capture=None):
-    """Route the model's attention through the stores of ``cache`` for the
-    duration of the block: ``backend='packed'`` runs :func:`packed_attention`
-    (the sm_100a decode kernels), ``'dense'`` the dequantise-then-attend path.
-    Without a cache the stock SDPA runs (queries can still be captured).  The
-    registry entry is pointed back at SDPA on exit so it keeps no cache alive."""
+def paged_route(model, cache, backend: str = "packed"):
+    """Route ``model``'s attention over ``cache``'s pages (one query token per
+    sequence) for the duration of the block: ``backend="packed"`` decodes with
+    :func:`packed_attention`, ``"dense"`` dequantises the pages and runs SDPA
+    (the reference route's two backends, colab_experiment.py:123-148).  On exit
+    the model's attention implementation is restored and the registry entry
+    points back at SDPA, so it keeps no reference to the cache."""
     from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
 
-    original = model.config._attn_implementation
-    dense_interface = ALL_ATTENTION_FUNCTIONS["sdpa"]
+    if backend not in ("packed", "dense"):
+        raise ValueError("backend must be 'packed' or 'dense'")
+    sdpa = ALL_ATTENTION_FUNCTIONS["sdpa"]
+    store = cache.store
 
     def attention(module, query, key, value, attention_mask, scaling, **kwargs):
-        if capture is not None:
-            capture[module.layer_idx] = query.detach().cpu()
-        if cache is None:
-            return dense_interface(module, query, key, value, attention_mask, scaling=scaling, **kwargs)
-        store = cache.stores[module.layer_idx]
+        if query.shape[2] != 1:
+            raise ValueError("the paged route decodes one token per sequence; prefill with the stock model")
         if backend == "packed":
-            result = packed_attention(query, store, scaling)
+            out = packed_attention(query, store.batch_view(module.layer_idx), scaling)
         else:
-            result = dense_attention(query, store, scaling)
-        return result.transpose(1, 2).contiguous(), None
+            k, v = store.dense(module.layer_idx)
+            g = query.shape[1] // k.shape[1]
+            out = torch.nn.functional.scaled_dot_product_attention(
+                query, k.repeat_interleave(g, 1), v.repeat_interleave(g, 1), scale=scaling)
+        return out.transpose(1, 2), None
 
+    previous = model.config._attn_implementation
     ALL_ATTENTION_FUNCTIONS.register(ROUTE, attention)
     model.config._attn_implementation = ROUTE
     try:
         yield
     finally:
-        model.config._attn_implementation = original
-        ALL_ATTENTION_FUNCTIONS.register(ROUTE, dense_interface)
+        model.config._attn_implementation = previous
+        ALL_ATTENTION_FUNCTIONS.register(ROUTE, sdpa)
 
 
-def forward_token(model, cache, token, packed=False):
-    """One decode step of ``token`` at the cache's current length."""
+def decode_step(model, cache, tokens: torch.Tensor):
+    """One batched decode step: ``tokens`` ``[batch]`` -> last-position logits ``[batch, vocab]``."""
     position = cache.get_seq_length()
-    return model(input_ids=torch.tensor([[token]], device=model.device), past_key_values=cache,
-                 cache_position=torch.tensor([position], device=model.device),
-                 attention_mask={"full_attention": None} if packed else None,
-                 use_cache=True, logits_to_keep=1)
-
-
-POLICY_BITS = {"paged_fp16": 16, "int8": 8, "int4": 4, "oracle": 4}
-
-
-@torch.inference_mode()
-def decode_logits(model, source, first_token, forced, settings, policy, protected=(), backend="packed"):
-    """Logits [steps, vocab] of a decode replay: ``first_token`` then the
-    ``forced`` tokens, over a stock cache (``policy='native_fp16'``) or a live
-    cache demoted to the policy's bits (the loop of colab_experiment.py:191-214)."""
-    native = policy == "native_fp16"
-    device = model.device
-    cache = stock_cache(source, device) if native else make_live_cache(
-        source, settings, protected, POLICY_BITS[policy], device=device)
-    logits = []
-    token = first_token
-    with attention_route(model, cache=None if native else cache, backend=backend):
-        for step in range(len(forced)):
-            output = forward_token(model, cache, token, packed=not native)
-            logits.append(output.logits[0, -1].float())
-            token = int(forced[step])
-    return torch.stack(logits)
-
-
-@torch.inference_mode()
-def model_gate(model, source, first_token, forced, settings):
-    """The reference's model gate (colab_experiment.py:294-313) on token ids:
-    for every policy the packed route must stay within a mean KL of 0.002 of
-    the dense route over the same stores, with finite logits; the FP16 paged
-    route must match the stock model.  Raises AssertionError otherwise and
-    returns the per-policy figures."""
-    stock = decode_logits(model, source, first_token, forced, settings, "native_fp16")
-    checks = []
-    for policy, protected in [("paged_fp16", ()), ("int8", ()), ("int4", ()), ("oracle", (0, 2))]:
-        dense = decode_logits(model, source, first_token, forced, settings, policy, protected, "dense")
-        packed = decode_logits(model, source, first_token, forced, settings, policy, protected, "packed")
-        discrepancy = float(kl_divergence(dense, packed).mean())
-        if discrepancy > 0.002 or not torch.isfinite(packed).all():
-            raise AssertionError(f"kernel/model mismatch for {policy}: KL={discrepancy}")
-        if policy == "paged_fp16":
-            torch.testing.assert_close(dense, stock, atol=0.05, rtol=0.01)
-            if float(kl_divergence(stock, packed).mean()) > 0.002:
-                raise AssertionError("FP16 packed route does not match the stock model")
-        checks.append({"policy": policy, "mean_kl_dense_vs_packed": discrepancy,
-                       "max_logit_error": float((dense - packed).abs().max())})
-    return checks
-
-
-CONTROLLED_POLICIES = ("native_fp16", "paged_fp16", "int8", "int4", "automatic", "recent", "random", "oracle")
-
-
-def controlled_decode(model, source, settings, policy, input_tokens, measured_tokens, warmup_tokens=32,
-                      protected=(), backend="packed"):
-    """Fixed-history decode throughput and cache lifecycle
-    (benchmark_suite.controlled_decode, benchmark_suite.py:155-264): the
-    ``warmup_tokens`` then ``measured_tokens`` of ``input_tokens`` are appended
-    one decode step at a time after the ``source`` prefix; no sampling, no
-    logit transfers.  ``measured_cuda_timeline_seconds`` is device-timeline
-    time between two events (launch gaps included).  Returns the reference's
-    row fields."""
-    import gc
-    import hashlib
-    import json
-    import time
-
-    total = warmup_tokens + measured_tokens
-    if warmup_tokens < 0 or measured_tokens <= 0 or len(input_tokens) != total:
-        raise ValueError("provide exactly warmup_tokens + measured_tokens input tokens")
-    if policy not in CONTROLLED_POLICIES:
-        raise ValueError("unknown policy")
-    device = model.device
-    gpu = device.type == "cuda"
-    if not gpu and backend == "packed" and policy != "native_fp16":
-        raise ValueError("packed throughput requires CUDA")
-    native = policy == "native_fp16"
-    bits = 16 if policy == "paged_fp16" else 8 if policy == "int8" else 4
-
-    def synchronize():
-        if gpu:
-            torch.cuda.synchronize(device)
-
-    def report(cache):
-        if not native:
-            return cache.report()
-        size = sum(t.numel() * t.element_size() for layer in cache.layers for t in (layer.keys, layer.values))
-        return {"tokens": cache.get_seq_length(), "resident_bytes": size, "payload_bytes": size, "demotions": 0}
-
-    gc.collect()
-    if gpu:
-        torch.cuda.empty_cache()
-    prefix = source[0][0].shape[-2]
-    ids = torch.tensor([input_tokens], device=device, dtype=torch.long)
-    positions = torch.arange(prefix, prefix + total, device=device)
-    synchronize()
-    base_allocated = torch.cuda.memory_allocated(device) if gpu else None
-    if gpu:
-        torch.cuda.reset_peak_memory_stats(device)
-    started = time.perf_counter()
-    with torch.inference_mode():
-        cache = (stock_cache(source, device=device) if native else
-                 make_live_cache(source, settings, protected, bits, max_tokens=prefix + total, device=device))
-        synchronize()
-        setup_seconds = time.perf_counter() - started
-        initial = report(cache)
-
-        def step(index):
-            output = model(input_ids=ids[:, index:index + 1], past_key_values=cache,
-                           cache_position=positions[index:index + 1], use_cache=True,
-                           attention_mask=None if native else {"full_attention": None}, logits_to_keep=1)
-            del output
-
-        with attention_route(model, None if native else cache, backend):
-            warm_started = time.perf_counter()
-            for index in range(warmup_tokens):
-                step(index)
-            synchronize()
-            warmup_seconds = time.perf_counter() - warm_started
-            before = report(cache)
-            setup_warmup_peak = torch.cuda.max_memory_allocated(device) if gpu else None
-            if gpu:
-                torch.cuda.reset_peak_memory_stats(device)
-                begin = torch.cuda.Event(enable_timing=True)
-                end = torch.cuda.Event(enable_timing=True)
-            measured_started = time.perf_counter()
-            if gpu:
-                begin.record()
-            for index in range(warmup_tokens, total):
-                step(index)
-            if gpu:
-                end.record()
-            synchronize()
-            wall_seconds = time.perf_counter() - measured_started
-            cuda_seconds = begin.elapsed_time(end) / 1000 if gpu else None
-        final = report(cache)
-        peak = torch.cuda.max_memory_allocated(device) if gpu else None
-        end_allocated = torch.cuda.memory_allocated(device) if gpu else None
-    assert final["tokens"] == prefix + total, "decode did not append the complete fixed workload"
-    row = {"policy": policy, "backend": "stock_sdpa" if native else backend,
-           "scope": "fixed-history throughput and cache lifecycle; not answer accuracy",
-           "prefix_tokens": prefix, "warmup_tokens": warmup_tokens, "measured_tokens": measured_tokens,
-           "setup_seconds": setup_seconds, "warmup_seconds": warmup_seconds,
-           "measured_wall_seconds": wall_seconds, "measured_cuda_timeline_seconds": cuda_seconds,
-           "steady_tokens_per_second": measured_tokens / wall_seconds,
-           "setup_warmup_decode_seconds": setup_seconds + warmup_seconds + wall_seconds,
-           "initial_cache": initial, "measurement_start_cache": before, "final_cache": final,
-           "new_measured_demotions": final["demotions"] - before["demotions"],
-           "setup_warmup_peak_allocated_bytes": setup_warmup_peak, "measured_peak_allocated_bytes": peak,
-           "measured_peak_incremental_bytes": peak - base_allocated if gpu else None,
-           "end_incremental_bytes": end_allocated - base_allocated if gpu else None,
-           "input_sha256": hashlib.sha256(json.dumps(input_tokens).encode()).hexdigest()}
-    del cache, ids, positions
-    gc.collect()
-    if gpu:
-        torch.cuda.empty_cache()
-    return row
+    out = model(input_ids=tokens.view(-1, 1), past_key_values=cache,
+                cache_position=torch.tensor([position], device=tokens.device),
+                attention_mask={"full_attention": None}, use_cache=True, logits_to_keep=1)
+    return out.logits[:, -1]

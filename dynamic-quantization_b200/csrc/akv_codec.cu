@@ -444,6 +444,57 @@ __global__ void __launch_bounds__(256) unpack_pages_kernel(const int64_t *__rest
   }
 }
 
+// ============================================================ token append
+// Write `rows` decode-step token rows of K and V for every sequence of a batch
+// into FP16 page records: sequence b's rows go to rows first_row .. of the page
+// its table entry (or, for a fresh page, new_desc[b]) names.  One warp per
+// (sequence, head, page row, K|V); a row is head_dim fp16 values, 8 bytes per
+// lane.  K rows are stored row-major, V rows in the bank-swizzled order
+// (v_swizzle keeps a row inside its own bytes, so an 8-byte chunk moves
+// whole).  A fresh page's other rows are zeroed, as the reference's new pages
+// start from zeros (packed_decode.py:141-146).  The entry's valid-token count
+// becomes first_row + rows; its mode and offset do not change, so warps that
+// read it while one warp rewrites it see the same page.
+template <int D>
+__global__ void __launch_bounds__(256) append_rows_kernel(
+    const __half *__restrict__ src_k, const __half *__restrict__ src_v, int64_t sbs, int64_t shs, int64_t sts,
+    int batch, int rows, int first_row, int64_t *table, int64_t table_stride, int page,
+    const int64_t *__restrict__ new_desc, uint8_t *__restrict__ arena, int64_t arena_bytes, int heads,
+    int32_t *status) {
+  constexpr int LANES = D / 4;  // lanes holding 4 values (8 bytes) of a row
+  constexpr int64_t RB = 2 * kBlock * D * 2;  // FP16 record: K and V payloads, no scales
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t items = (int64_t)batch * heads * kBlock * 2;
+  for (int64_t it = warp; it < items; it += nwarps) {
+    const int kv = (int)(it & 1);
+    const int r = (int)((it >> 1) % kBlock);
+    const int h = (int)((it >> 1) / kBlock % heads);
+    const int b = (int)((it >> 1) / kBlock / heads);
+    int64_t *entry = table + (int64_t)b * table_stride + page;
+    const int64_t d = new_desc ? new_desc[b] : *entry;
+    if (desc_mode(d) != AKV_MODE_FP16 || !page_in_arena(d, RB * heads, arena_bytes)) {
+      if (lane == 0 && h == 0 && r == 0 && kv == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+      continue;
+    }
+    const bool written = r >= first_row && r < first_row + rows;
+    if (!written && !new_desc) continue;
+    uint8_t *pay = arena + desc_offset(d) + h * RB + kv * (kBlock * D * 2);
+    if (lane < LANES) {
+      uint2 v = make_uint2(0u, 0u);
+      if (written) {
+        const __half *src = (kv ? src_v : src_k) + b * sbs + h * shs + (int64_t)(r - first_row) * sts;
+        v = *reinterpret_cast<const uint2 *>(src + 4 * lane);
+      }
+      const int64_t o = (int64_t)r * (2 * D) + 8 * lane;
+      *reinterpret_cast<uint2 *>(pay + (kv ? v_swizzle(D, AKV_MODE_FP16, o) : o)) = v;
+    }
+    if (lane == 0 && h == 0 && r == 0 && kv == 0)
+      *entry = (d & ~((int64_t)15 << 2)) | ((int64_t)(first_row + rows - 1) << 2);
+  }
+}
+
 // ================================================================ launchers
 static int grid_for(int64_t warps_needed) {
   int dev = 0, sms = 148;
@@ -637,4 +688,27 @@ extern "C" int akv_unpack_pages(const int64_t *desc, int64_t n_pages, const void
                (cudaStream_t)stream};
   return head_dim == 64 ? dispatch_group<64, UnpackLaunch>(group, a)
                         : dispatch_group<128, UnpackLaunch>(group, a);
+}
+
+extern "C" int akv_append_rows(const void *src_k, const void *src_v, int64_t src_batch_stride,
+                               int64_t src_head_stride, int64_t src_token_stride, int batch, int rows,
+                               int first_row, int64_t *table, int64_t table_stride, int page,
+                               const int64_t *new_desc, void *arena, int64_t arena_bytes, int heads,
+                               int head_dim, int32_t *dev_status, void *stream) {
+  if (head_dim != 64 && head_dim != 128) return AKV_ERR_UNSUPPORTED;
+  if (!src_k || !src_v || !table || !arena || batch <= 0 || heads <= 0 || page < 0) return AKV_ERR_INVALID;
+  if (rows <= 0 || first_row < 0 || first_row + rows > kBlock || table_stride <= page) return AKV_ERR_INVALID;
+  if (((uintptr_t)src_k & 7) || ((uintptr_t)src_v & 7) || !aligned16(arena)) return AKV_ERR_INVALID;
+  if (src_batch_stride % 4 || src_head_stride % 4 || src_token_stride % 4) return AKV_ERR_INVALID;
+  const int grid = grid_for((int64_t)batch * heads * kBlock * 2);
+  cudaStream_t s = (cudaStream_t)stream;
+#define AKV_APPEND(D)                                                                                     \
+  append_rows_kernel<D><<<grid, 256, 0, s>>>((const __half *)src_k, (const __half *)src_v, src_batch_stride, \
+                                             src_head_stride, src_token_stride, batch, rows, first_row, table,  \
+                                             table_stride, page, new_desc, (uint8_t *)arena, arena_bytes, heads, \
+                                             dev_status)
+  if (head_dim == 64) AKV_APPEND(64);
+  else AKV_APPEND(128);
+#undef AKV_APPEND
+  return launch_status();
 }

@@ -129,6 +129,22 @@ int akv_repack_pages(const int64_t *src_desc, const int64_t *dst_desc, int64_t n
                      void *arena, int64_t arena_bytes, int heads, int head_dim, int group,
                      int semantics, int32_t *dev_status, void *stream);
 
+/* Append decode-step tokens of a batch into FP16 pages: for every sequence b,
+ * `rows` token rows of src_k/src_v (fp16 [batch][heads][rows][head_dim] with
+ * the given strides in elements, head_dim contiguous, 8-byte aligned) are
+ * written at page rows first_row .. first_row + rows - 1 of the page named by
+ * table[b * table_stride + page], whose valid-token count becomes
+ * first_row + rows.  new_desc (nullable): a fresh FP16 page per sequence, whose
+ * descriptor is written into the table first and whose other rows are zeroed.
+ * first_row + rows <= 16.  Replaces the per-token page writes and the
+ * host-to-device publish of PagedLayer.append (packed_decode.py:126-154), for a
+ * batch of sequences in one launch. */
+int akv_append_rows(const void *src_k, const void *src_v, int64_t src_batch_stride,
+                    int64_t src_head_stride, int64_t src_token_stride, int batch, int rows,
+                    int first_row, int64_t *table, int64_t table_stride, int page,
+                    const int64_t *new_desc, void *arena, int64_t arena_bytes, int heads,
+                    int head_dim, int32_t *dev_status, void *stream);
+
 /* Dequantize pages to dense out_k/out_v[heads][n_pages*16][head_dim] of
  * out_dtype (skipped pages read as zeros): AKV_DTYPE_F16 gives
  * fp16(int * float(scale)) as QuantizedPage.dense; AKV_DTYPE_F32 / _BF16 round
