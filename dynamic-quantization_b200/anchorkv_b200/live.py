@@ -112,6 +112,7 @@ class PagedKVStore:
                   batch * n, d.data_ptr(), self.pool.arena.data_ptr(), self.pool.nbytes, heads, dim, self.group,
                   _lib.SEM_PAGE, _lib.status_ptr(self.device), _lib.stream_of(self.device))
         self.tables[layer, :, :n].copy_(d.view(batch, n))
+        self.demotions += batch * int((bits != 16).sum())  # the reference appends, then demotes, these pages
         self._desc[layer, :, :n] = desc
         self.lengths[layer] = tokens
         self._archived[layer] = max(eligible - 1, -1)

@@ -478,6 +478,8 @@ __global__ void __launch_bounds__(256) append_rows_kernel(
       if (lane == 0 && h == 0 && r == 0 && kv == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
       continue;
     }
+    if (lane == 0 && h == 0 && r == 0 && kv == 0)  // one warp per sequence publishes the new count
+      *entry = (d & ~((int64_t)15 << 2)) | ((int64_t)(first_row + rows - 1) << 2);
     const bool written = r >= first_row && r < first_row + rows;
     if (!written && !new_desc) continue;
     uint8_t *pay = arena + desc_offset(d) + h * RB + kv * (kBlock * D * 2);
@@ -490,8 +492,6 @@ __global__ void __launch_bounds__(256) append_rows_kernel(
       const int64_t o = (int64_t)r * (2 * D) + 8 * lane;
       *reinterpret_cast<uint2 *>(pay + (kv ? v_swizzle(D, AKV_MODE_FP16, o) : o)) = v;
     }
-    if (lane == 0 && h == 0 && r == 0 && kv == 0)
-      *entry = (d & ~((int64_t)15 << 2)) | ((int64_t)(first_row + rows - 1) << 2);
   }
 }
 

@@ -121,15 +121,15 @@ def test_requantize_is_one_repack_and_frees_pages(cuda):
     assert pool.free_slots(4) >= 5
     after = akv.packed_attention(q, cache, 0.088)
     assert not torch.equal(before, after)
-    cache.feed_declarations("<local>")  # sink and response only
+    cache.feed_declarations("<local>")  # sink, scaffold and response only
     local = akv.packed_attention(q, cache, 0.088)
     mat = cache.materialize_visible()
     g = spec["q_heads"] // mat.key.shape[1]
     want = torch.nn.functional.scaled_dot_product_attention(
         q, mat.key.repeat_interleave(g, 1), mat.value.repeat_interleave(g, 1), scale=0.088)
     torch.testing.assert_close(local, want, atol=ATOL, rtol=RTOL)
-    cache.requantize_segment(0, CacheMode.EVICTED)
-    cache.requantize_segment(5, CacheMode.EVICTED)
+    for sid in (0, 1, 5):  # the sink, scaffold and response segments <local> keeps visible
+        cache.requantize_segment(sid, CacheMode.EVICTED)
     with pytest.raises(RuntimeError, match="no resident"):  # every visible block is evicted
         cache.decode_view(0)
     assert akv.take_device_status(cuda) == 0

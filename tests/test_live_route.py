@@ -99,7 +99,7 @@ def test_reference_model_gate_with_this_package(cuda, reference, head_dim, heads
     colab_experiment, _ = reference
     model = _qwen3(head_dim, heads, kv_heads, 4, cuda, torch.float16)
     ids = torch.randint(0, 2048, (181,), generator=torch.Generator().manual_seed(2)).tolist()
-    case = {"ids": ids, "answer": "4821"}
+    case = {"ids": ids, "answer": "4821", "case_id": "random-qwen3"}
     source = colab_experiment.prefill_case(model, case)
     checks = colab_experiment.model_gate(model, _DigitTokenizer(), source, case, colab_experiment.Settings())
     assert [c["policy"] for c in checks] == ["paged_fp16", "int8", "int4", "oracle"]
