@@ -1072,6 +1072,298 @@ def run_reference_gpu(args):
         torch.cuda.empty_cache()
 
 
+# ----------------------------------------------------------- live decode
+LIVE_PREFIXES = (128, 256, 512)
+
+
+def _qwen3_06b(device):
+    """Randomly initialised Qwen3-0.6B architecture (no checkpoint offline): 28
+    layers, hidden 1024, 16 query / 8 KV heads of 128, fp16."""
+    import torch
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    torch.manual_seed(0)
+    config = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                         num_attention_heads=16, num_key_value_heads=8, head_dim=128,
+                         max_position_embeddings=40960, tie_word_embeddings=True, attn_implementation="sdpa")
+    return Qwen3ForCausalLM(config).to(device=device, dtype=torch.float16).eval()
+
+
+def run_live(args):
+    """Decode tokens/s of a Qwen3-0.6B-shaped model (random weights) at
+    128/256/512-token prefixes, one JSON line per (arm, prefix):
+
+    * reference: the reference's controlled_decode (benchmark_suite.py:155-264)
+      with its own live cache and packed route (its PagedLayer and Triton
+      kernel, installed unmodified in baseline/_ref), INT4 archive;
+    * ours_dropin: the same harness with this package's PagedLayer,
+      dense_attention and packed_attention substituted for the reference's;
+    * stock: the harness's native_fp16 policy (transformers SDPA, FP16 cache);
+    * ours_batched: this package's batched live cache (anchorkv_b200.live) at
+      batch 1 and 32, INT4 archive; tokens/s counts every sequence's token.
+
+    Each arm decodes the same fixed token history (32 warm-up, --live-tokens
+    measured) after the same prefill, timed as the harness times it (wall
+    clock and CUDA events around the measured steps)."""
+    import torch
+
+    import anchorkv_b200 as akv
+    from anchorkv_b200 import live
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ref_pd, why = import_reference()
+    if ref_pd is None:
+        print(json.dumps({"workload": "live", "unavailable": why}), flush=True)
+        return
+    from anchorkv import benchmark_suite as BS
+    from anchorkv import colab_experiment as CE
+    from anchorkv import triton_decode as TD
+
+    model = _qwen3_06b(dev)
+    settings = CE.Settings()
+    warm, measured = 32, args.live_tokens
+    gen = torch.Generator().manual_seed(11)
+    originals = (CE.PagedLayer, CE.dense_attention, CE.pack_page, TD.packed_attention)
+
+    def substitute(ours):
+        CE.PagedLayer, CE.dense_attention, CE.pack_page, TD.packed_attention = (
+            (akv.PagedLayer, akv.dense_attention, akv.pack_page, akv.packed_attention) if ours else originals)
+
+    for prefix in LIVE_PREFIXES:
+        ids = torch.randint(0, 151936, (1, prefix), generator=gen)
+        tokens = torch.randint(0, 151936, (warm + measured,), generator=gen).tolist()
+        with torch.inference_mode():
+            out = model(input_ids=ids.to(dev), use_cache=True, logits_to_keep=1)
+            source = CE.cache_cpu(out.past_key_values)
+            del out
+        for arm, policy, ours in (("reference", "int4", False), ("ours_dropin", "int4", True),
+                                  ("stock", "native_fp16", False)):
+            substitute(ours)
+            try:
+                row = BS.controlled_decode(model, source, settings, policy, tokens, measured, warmup_tokens=warm)
+            finally:
+                substitute(False)
+            line = {"workload": "live controlled decode, Qwen3-0.6B shape (random weights), batch 1",
+                    "arm": arm, "prefix_tokens": prefix, "batch": 1, "measured_tokens": measured,
+                    "tokens_per_s": round(row["steady_tokens_per_second"], 2),
+                    "cuda_timeline_tokens_per_s": round(measured / row["measured_cuda_timeline_seconds"], 2),
+                    "final_payload_bytes": row["final_cache"]["payload_bytes"],
+                    "new_measured_demotions": row["new_measured_demotions"]}
+            print(json.dumps(line), flush=True)
+        for batch in (1, 32):
+            seqs = [(k.expand(batch, -1, -1, -1).contiguous().to(dev), v.expand(batch, -1, -1, -1).contiguous().to(dev))
+                    for k, v in source]
+            hist = torch.tensor(tokens, device=dev).view(1, -1).expand(batch, -1).contiguous()
+            with torch.inference_mode():
+                cache = live.batched_live_cache(seqs, max_tokens=prefix + warm + measured + 16, device=dev)
+                with live.paged_route(model, cache):
+                    for i in range(warm):
+                        live.decode_step(model, cache, hist[:, i])
+                    torch.cuda.synchronize(dev)
+                    t0 = time.perf_counter()
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    for i in range(warm, warm + measured):
+                        live.decode_step(model, cache, hist[:, i])
+                    b.record()
+                    torch.cuda.synchronize(dev)
+                    wall = time.perf_counter() - t0
+            assert akv.take_device_status(dev) == 0
+            line = {"workload": f"live decode, Qwen3-0.6B shape (random weights), batch {batch}",
+                    "arm": "ours_batched", "prefix_tokens": prefix, "batch": batch, "measured_tokens": measured,
+                    "tokens_per_s": round(batch * measured / wall, 2),
+                    "cuda_timeline_tokens_per_s": round(batch * measured / (a.elapsed_time(b) / 1e3), 2),
+                    "final_payload_bytes": cache.report()["payload_bytes"],
+                    "demotions": cache.report()["demotions"]}
+            print(json.dumps(line), flush=True)
+            del cache, seqs
+
+
+# --------------------------------------------------------- other kernels
+def run_kernels(args):
+    """Every kernel besides the decode and the pack, on a case larger than L2
+    (or, for the merges, the decode's own partials, which L2 holds), timed with
+    CUDA events over --steps launches after --warmup: one JSON line per kernel
+    with its algorithmic bytes, achieved GB/s and fraction of the measured HBM
+    peak.  --kernel NAME runs one case (the ncu captures do)."""
+    import numpy as np
+    import torch
+
+    import anchorkv_b200 as akv
+    from anchorkv_b200 import _lib
+    from anchorkv_b200 import live as LV
+    from anchorkv_b200 import pool as P
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    status = _lib.status_word(dev).data_ptr()
+    peak, peak_kind = hbm_peak()
+    wanted = args.kernel
+    import ctypes
+
+    def timed(name, nbytes, fn, note):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, b in ev:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = sum(a.elapsed_time(b) for a, b in ev) / len(ev)
+        assert akv.take_device_status(dev) == 0
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"workload": "kernels", "kernel": name, "launch_ms_mean": round(ms, 5),
+                          "algorithmic_bytes_per_launch": int(nbytes), "achieved_gbs": round(gbs, 1),
+                          "frac_of_hbm_peak": round(gbs / peak, 4), "peak": peak,
+                          "peak_source": f"{peak_kind} hbm_gbs", "case": note}), flush=True)
+
+    def want(name):
+        return wanted in (None, name)
+
+    if want("quantize_flat") or want("dequantize_flat"):
+        n = 256 << 20  # 256 Mi fp16 elements (512 MB), groups of 64, INT4
+        x = torch.randn(n, dtype=torch.float16, device=dev)
+        payload = torch.empty(n // 2, dtype=torch.uint8, device=dev)
+        scales = torch.empty(n // 64, dtype=torch.float16, device=dev)
+        out = torch.empty_like(x)
+        q_bytes = 2 * n + n // 2 + 2 * (n // 64)
+        if want("quantize_flat"):
+            timed("quantize_flat_kernel<half,4,tensor>", q_bytes,
+                  lambda: _lib.call("akv_quantize", x.data_ptr(), _lib.DTYPE_F16, n, 64, 4, _lib.SEM_TENSOR,
+                                    payload.data_ptr(), scales.data_ptr(), sptr),
+                  "256 Mi fp16 elements to INT4, group 64 (quantize_tensor)")
+        if want("dequantize_flat"):
+            _lib.call("akv_quantize", x.data_ptr(), _lib.DTYPE_F16, n, 64, 4, _lib.SEM_TENSOR, payload.data_ptr(),
+                      scales.data_ptr(), sptr)
+            timed("dequantize_flat_kernel<half,4>", q_bytes,
+                  lambda: _lib.call("akv_dequantize", payload.data_ptr(), scales.data_ptr(), n, 64, 4,
+                                    out.data_ptr(), _lib.DTYPE_F16, sptr),
+                  "256 Mi INT4 elements to fp16, group 64 (PackedTensor.dequantize)")
+        del x, payload, scales, out
+    if want("unpack_pages") or want("repack_pages"):
+        wl = WORKLOADS["batched_small"]
+        pool, layers, _, kv_bytes = build_workload(wl, dev, seed=1234, batch=16, distinct=1)
+        t = layers[0]
+        desc = t.table.reshape(-1).contiguous()
+        npg = desc.numel()
+        if want("unpack_pages"):
+            ok = torch.empty((wl["kv_heads"], npg * 16, wl["dim"]), dtype=torch.float16, device=dev)
+            ov = torch.empty_like(ok)
+            dense = 2 * ok.numel() * 2
+            timed("unpack_pages_kernel<128,2048,half>", kv_bytes[0] + dense,
+                  lambda: _lib.call("akv_unpack_pages", desc.data_ptr(), npg, pool.arena.data_ptr(), pool.nbytes,
+                                    wl["kv_heads"], wl["dim"], wl["group"], ok.data_ptr(), ov.data_ptr(),
+                                    _lib.DTYPE_F16, status, sptr),
+                  "one layer of the batched workload at 16 sequences (8192 tokens, 15/35/40/10 mix) to dense fp16")
+            del ok, ov
+        if want("repack_pages"):
+            d = desc.cpu().numpy()
+            src = d[(d & 3) == _lib.MODE_FP16]  # the FP16 pages, requantized to INT4
+            pool.reserve(4, src.size)
+            dst_off = pool.alloc_many(4, src.size)
+            dst = P.encode_array(np.full(src.size, _lib.MODE_INT4), np.full(src.size, 16), dst_off)
+            s_t, d_t = torch.from_numpy(src).to(dev), torch.from_numpy(dst).to(dev)
+            nbytes = src.size * wl["kv_heads"] * (P.algorithmic_record_bytes(wl["dim"], wl["group"], 16) +
+                                                 P.algorithmic_record_bytes(wl["dim"], wl["group"], 4))
+            timed("pack_pages_kernel<128,2048,tensor,record>", nbytes,
+                  lambda: _lib.call("akv_repack_pages", s_t.data_ptr(), d_t.data_ptr(), src.size,
+                                    pool.arena.data_ptr(), pool.nbytes, wl["kv_heads"], wl["dim"], wl["group"],
+                                    _lib.SEM_TENSOR, status, sptr),
+                  f"{src.size} FP16 pages (8 KV heads) requantized to INT4 records (requantize_segment)")
+        del pool, layers
+    if want("merge_states"):
+        n, batch, hq, dim = 8, 4096, 32, 128
+        states = torch.randn((n, batch, hq, dim + 2), dtype=torch.float32, device=dev)
+        states[..., dim] = states[..., dim].abs()
+        out = torch.empty((batch, hq, 1, dim), dtype=torch.float16, device=dev)
+        timed("merge_states_kernel<128>", states.numel() * 4 + out.numel() * 2,
+              lambda: _lib.call("akv_merge_states", states.data_ptr(), n, batch, hq, dim, out.data_ptr(),
+                                out.stride(0), out.stride(1), sptr),
+              "8 states (8 GPUs' shares) of 4096 sequences x 32 query heads")
+        del states, out
+    if want("merge_wide") or want("merge_exchange") or want("merge_rows"):
+        for name in ("merge_wide", "merge_exchange", "merge_rows"):
+            if not want(name):
+                continue
+            if name == "merge_rows":
+                wl = WORKLOADS["batched_small"]
+                pool, layers, qs, _ = build_workload(wl, dev, seed=1234, distinct=1)
+                store, q, hq, hkv, D, batch, splits = layers[0], qs[0], wl["q_heads"], wl["kv_heads"], wl["dim"], \
+                    wl["batch"], wl["splits"]
+            else:
+                pool, store, _ = build_long_shard(LONG, dev, 0, 1)
+                hq, hkv, D, batch, splits = LONG["q_heads"], LONG["kv_heads"], LONG["dim"], 1, 0
+                q = torch.randn((1, hq, 1, D), device=dev).half()
+            mb = store.max_blocks
+            ws_bytes = lib.akv_workspace_bytes(batch, hq, hkv, D, mb, splits)
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+            out = torch.empty((batch, hq, 1, D), dtype=torch.float16, device=dev)
+            _lib.call("akv_decode_partials", pool.arena.data_ptr(), pool.nbytes, store.table.data_ptr(),
+                      store.table.stride(0), store.seq_blocks.data_ptr(), mb, q.data_ptr(), q.stride(0), q.stride(1),
+                      batch, hq, hkv, D, 2048, 0.088, splits, ws.data_ptr(), ws_bytes, status, sptr)
+            torch.cuda.synchronize(dev)
+            # bytes the merge reads: the partial states the decode wrote (every contributor of every row)
+            hdr = ws[:64].view(torch.int32).cpu().numpy().astype(np.int64)
+            warps, rng, items, slot_heads = hdr[1], hdr[3], hdr[5], hdr[10]
+            begin = np.arange(warps) * rng
+            end = np.minimum(begin + rng, items * mb)
+            touched = int(((end - 1) // mb - begin // mb + 1).sum())  # (warp, item) partials the merge folds
+            part = touched * slot_heads * (D + 2) * 4
+            if name == "merge_exchange":
+                nbytes_ex = lib.akv_exchange_bytes(1, batch, hq, D)
+                own = ctypes_alloc(nbytes_ex)
+                peers = (ctypes.c_void_p * 1)(own)
+                epoch = [0]
+
+                def fn():
+                    epoch[0] += 1
+                    _lib.call("akv_merge_exchange", ws.data_ptr(), batch, hq, D, peers, 0, 1, epoch[0],
+                              out.data_ptr(), out.stride(0), out.stride(1), status, sptr)
+
+                timed("merge_exchange_kernel<128>", part + out.numel() * 2, fn,
+                      "one rank's merge + exchange of the 1M-token sequence's partials (world 1: its own buffer)")
+                torch.cuda.synchronize(dev)
+                _lib.call("akv_ipc_free", ctypes.c_void_p(own))
+            else:
+                timed(f"{name}_kernel<128>", part + out.numel() * 2,
+                      lambda: _lib.call("akv_merge", ws.data_ptr(), batch, hq, D, out.data_ptr(), out.stride(0),
+                                        out.stride(1), None, status, sptr),
+                      "the decode's partials of " + ("the 1M-token sequence (one CTA per row)" if name != "merge_rows"
+                                                    else "one batched layer (one warp per row)") +
+                      "; L2 holds them (written by the decode just before)")
+            del pool, store, ws
+    if want("append_rows"):
+        batch, heads, dim = 1024, 8, 128
+        store = LV.PagedKVStore(1, batch, heads, dim, 4096, device=dev)
+        k = torch.randn((batch, heads, 64, dim), device=dev).half()
+        store.prefill(0, k, k)
+        kk = torch.randn((batch, heads, 1, dim), device=dev).half()
+        tbl = store.tables[0]
+        page, row = divmod(store.lengths[0], 16)
+        timed("append_rows_kernel<128>", 2 * kk.numel() * 2 * 2,
+              lambda: _lib.call("akv_append_rows", kk.data_ptr(), kk.data_ptr(), kk.stride(0), kk.stride(1),
+                                kk.stride(2), batch, 1, 3, tbl.data_ptr(), tbl.stride(0), page - 1, None,
+                                store.pool.arena.data_ptr(), store.pool.nbytes, heads, dim, status, sptr),
+              "one decode token of 1024 sequences x 8 KV heads into their FP16 pages (row 3)")
+
+
+def ctypes_alloc(nbytes: int) -> int:
+    """A zeroed device buffer from akv_ipc_alloc (the exchange buffers' allocator)."""
+    import ctypes
+
+    from anchorkv_b200 import _lib
+
+    ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+    _lib.call("akv_ipc_alloc", nbytes, ctypes.byref(ptr), handle)
+    return ptr.value
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1, help="GPUs of one node, one process each (torchrun for N > 1)")
@@ -1080,7 +1372,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference", "reference_gpu"), default="ours",
                     help="ours: the CUDA kernels; reference: the reference's CPU decode path (timed on the "
                          "host cores); reference_gpu: the reference's own Triton decode beside ours, batch 1")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["long", "pack", "pack_small"], default="batched",
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["long", "pack", "pack_small", "live", "kernels"],
+                    default="batched",
                     help="batched (default), large, long (one 1M-token sequence), pack (requantize); "
                          "*_small: one-layer profiling cases")
     ap.add_argument("--mix", choices=("fp16", "int8", "int4"), default=None,
@@ -1091,9 +1384,17 @@ def main():
                     help="skip the long-context leg of the batched/large runs (profiling runs)")
     ap.add_argument("--sustained-seconds", type=float, default=1.2,
                     help="seconds of back-to-back steps in the line's sustained record")
+    ap.add_argument("--kernel", default=None, help="--workload kernels: run this one case (e.g. unpack_pages)")
+    ap.add_argument("--live-tokens", type=int, default=64, help="--workload live: measured decode tokens")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
+    if args.workload == "live":
+        run_live(args)
+        return
+    if args.workload == "kernels":
+        run_kernels(args)
+        return
     if args.impl == "reference_gpu":
         run_reference_gpu(args)
         return
