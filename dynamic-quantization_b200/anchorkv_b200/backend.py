@@ -578,7 +578,7 @@ class DeclarativeKVCache:
             if seg.paged and seg.record.segment_id in visible and seg.mode is not CacheMode.EVICTED:
                 keep[seg.columns] = True
         host = np.where(keep[None, :], self._descriptors[:, :self._columns], 0)
-        table = _to_device(host, self._pool.device)
+        table = P.to_device(host, self._pool.device)
         self._device_table = (key, table)
         return table
 
@@ -614,7 +614,7 @@ class DeclarativeKVCache:
         ntok = np.broadcast_to(np.array(seg.lengths, np.int64), (rows, nblk))
         desc = P.encode_array(np.full((rows, nblk), _lib.MODE_FP16), ntok, slots)
         dev = self._pool.device
-        d = _to_device(desc.reshape(-1), dev)
+        d = P.to_device(desc.reshape(-1), dev)
         _lib.call("akv_pack_pages", k.data_ptr(), v.data_ptr(), heads * nblk * P.BLOCK * seg.dim,
                   nblk * P.BLOCK * seg.dim, nblk, rows * nblk, d.data_ptr(), self._pool.arena.data_ptr(),
                   self._pool.nbytes, heads, seg.dim, self.group_size, _lib.SEM_TENSOR, _lib.status_ptr(dev),
@@ -643,7 +643,7 @@ class DeclarativeKVCache:
             fresh = self._pool.alloc_many(bits, old.size).reshape(old.shape)
             new = P.encode_array(np.full(old.shape, P.BITS_TO_MODE[bits]), ((old >> 2) & 15) + 1, fresh)
             dev = self._pool.device
-            src, dst = _to_device(old.reshape(-1), dev), _to_device(new.reshape(-1), dev)
+            src, dst = P.to_device(old.reshape(-1), dev), P.to_device(new.reshape(-1), dev)
             heads = self._table_geometry[0][-1]
             _lib.call("akv_repack_pages", src.data_ptr(), dst.data_ptr(), old.size, self._pool.arena.data_ptr(),
                       self._pool.nbytes, heads, seg.dim, self.group_size, _lib.SEM_TENSOR, _lib.status_ptr(dev),
@@ -661,7 +661,7 @@ class DeclarativeKVCache:
         kernel_dtype = out_dtype if out_dtype in _KERNEL_DTYPES else torch.float32
         lead, dim, dev = self._table_geometry
         rows, heads, n = self._descriptors.shape[0], lead[-1], len(cols)
-        desc = _to_device(self._descriptors[:, cols].reshape(-1), dev)
+        desc = P.to_device(self._descriptors[:, cols].reshape(-1), dev)
         k = torch.empty((heads, rows * n * P.BLOCK, dim), dtype=kernel_dtype, device=dev)
         v = torch.empty_like(k)
         _lib.call("akv_unpack_pages", desc.data_ptr(), rows * n, self._pool.arena.data_ptr(), self._pool.nbytes,
@@ -722,12 +722,6 @@ class DeclarativeKVCache:
             return self._segments[segment_id]
         except KeyError as error:
             raise KeyError(f"unknown segment {segment_id}") from error
-
-
-def _to_device(array: np.ndarray, device) -> torch.Tensor:
-    """An int64 host array on ``device`` through pinned memory, without blocking
-    the host (torch keeps the pinned block until the copy has run)."""
-    return torch.from_numpy(np.ascontiguousarray(array)).pin_memory().to(device, non_blocking=True)
 
 
 def _tensor_bytes(tensor: Any | None) -> int:

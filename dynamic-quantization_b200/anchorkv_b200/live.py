@@ -107,7 +107,7 @@ class PagedKVStore:
         pad = n * P.BLOCK - tokens
         k = torch.nn.functional.pad(key.half(), (0, 0, 0, pad)).contiguous()
         v = torch.nn.functional.pad(value.half(), (0, 0, 0, pad)).contiguous()
-        d = _to_device(desc.reshape(-1), self.device)
+        d = P.to_device(desc.reshape(-1), self.device)
         _lib.call("akv_pack_pages", k.data_ptr(), v.data_ptr(), heads * n * P.BLOCK * dim, n * P.BLOCK * dim, n,
                   batch * n, d.data_ptr(), self.pool.arena.data_ptr(), self.pool.nbytes, heads, dim, self.group,
                   _lib.SEM_PAGE, _lib.status_ptr(self.device), _lib.stream_of(self.device))
@@ -125,7 +125,7 @@ class PagedKVStore:
         rows = key.shape[2]
         if self.lengths[layer] + rows > self.capacity * P.BLOCK:
             raise ValueError("cache geometry or capacity exceeded")
-        key, value = _halves(key), _halves(value)
+        key, value = P.as_fp16_rows(key), P.as_fp16_rows(value)
         status, stream = _lib.status_ptr(self.device), _lib.stream_of(self.device)
         done = 0
         while done < rows:
@@ -136,7 +136,7 @@ class PagedKVStore:
                 self.pool.reserve(16, self.batch)
                 offs = self.pool.alloc_many(16, self.batch)
                 new = P.encode_array(np.full(self.batch, _lib.MODE_FP16), np.full(self.batch, take), offs)
-                fresh = _to_device(new, self.device)
+                fresh = P.to_device(new, self.device)
                 self._desc[layer, :, page] = new
             else:
                 self._desc[layer, :, page] = (self._desc[layer, :, page] & ~np.int64(15 << 2)) | ((row + take - 1) << 2)
@@ -161,11 +161,11 @@ class PagedKVStore:
         offs = self.pool.alloc_many(self.archive_bits, src.size)
         dst = P.encode_array(np.full(src.shape, P.BITS_TO_MODE[self.archive_bits]), ((src >> 2) & 15) + 1,
                              offs.reshape(src.shape))
-        s_dev, d_dev = _to_device(src.reshape(-1), self.device), _to_device(dst.reshape(-1), self.device)
+        s_dev, d_dev = P.to_device(src.reshape(-1), self.device), P.to_device(dst.reshape(-1), self.device)
         _lib.call("akv_repack_pages", s_dev.data_ptr(), d_dev.data_ptr(), src.size, self.pool.arena.data_ptr(),
                   self.pool.nbytes, self.heads, self.dim, self.group, _lib.SEM_PAGE, _lib.status_ptr(self.device),
                   _lib.stream_of(self.device))
-        self.tables[layer][:, pages] = d_dev.view(src.shape)
+        self.tables[layer].index_copy_(1, P.to_device(pages, self.device), d_dev.view(src.shape))
         self._desc[layer][:, pages] = dst
         self.pool.free_many(16, src >> 8)  # stream order: later writes to these slots follow the repack
         self.demotions += src.size
@@ -216,20 +216,6 @@ class PagedKVStore:
     def report(self) -> dict:
         return {"resident_bytes": self.resident_bytes, "payload_bytes": self.payload_bytes,
                 "demotions": self.demotions, "tokens": self.lengths[0], "batch": self.batch}
-
-
-def _halves(t: torch.Tensor) -> torch.Tensor:
-    """fp16 with head_dim contiguous and 8-byte aligned rows (akv_append_rows' input)."""
-    t = t.to(torch.float16)
-    if t.stride(-1) != 1 or t.data_ptr() % 8 or any(s % 4 for s in t.stride()[:3]):
-        t = t.contiguous()
-    return t
-
-
-def _to_device(array: np.ndarray, device) -> torch.Tensor:
-    """An int64 host array on ``device`` through pinned memory, without blocking
-    the host (torch keeps the pinned block until the copy has run)."""
-    return torch.from_numpy(np.ascontiguousarray(array, np.int64)).pin_memory().to(device, non_blocking=True)
 
 
 _CACHE_CLASS = None

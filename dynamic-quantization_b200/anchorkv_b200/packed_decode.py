@@ -23,7 +23,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
-from .pool import BLOCK, PagePool, encode, group_ok, record_bytes, v_order
+from .pool import BLOCK, PagePool, as_fp16_rows, encode, group_ok, record_bytes, to_device, v_order
 
 
 def tensor_bytes(tensor) -> int:
@@ -174,11 +174,6 @@ class PagedLayer:
             out.append(QuantizedPage(bits, data, scales, shape, self.group, order=order))
         return tuple(out)
 
-    def _publish(self, page: int) -> None:
-        bits, offset = self._slots[page]
-        ntok = min(BLOCK, self.length - page * BLOCK) if page * BLOCK < self.length else BLOCK
-        self.table[page] = encode(bits, max(ntok, 1), offset)
-
     # ------------------------------------------------------------------ API
     def append(self, key, value):
         if key.shape != value.shape or key.ndim != 4 or key.shape[:2] != (1, self.heads):
@@ -186,21 +181,27 @@ class PagedLayer:
         if key.shape[-1] != self.dim or self.length + key.shape[-2] > self.capacity * self.block:
             raise ValueError('cache geometry or capacity exceeded')
         _lib.require_cuda(key, "key")
+        key, value = as_fp16_rows(key), as_fp16_rows(value)
+        dev = self.device
         offset = 0
         while offset < key.shape[-2]:
             page, position = divmod(self.length, self.block)
-            if position == 0:
+            take = min(self.block - position, key.shape[-2] - offset)
+            fresh = None
+            if position == 0:  # a new FP16 page: its descriptor reaches the table in the append launch
                 slot = self.pool.alloc(16)
-                self.pool.page_view(slot, 16).zero_()
                 self._slots.append((16, slot))
                 self.pages.append(self._views(16, slot))
-            take = min(self.block - position, key.shape[-2] - offset)
-            kpage, vpage = self.pages[page]
-            kpage.write_rows(position, key[0, :, offset:offset + take])
-            vpage.write_rows(position, value[0, :, offset:offset + take])
+                fresh = to_device([encode(16, take, slot)], dev)
+            k, v = key[:, :, offset:offset + take], value[:, :, offset:offset + take]
+            # one launch writes the rows (V in the stored byte order), zeroes the
+            # rest of a fresh page and moves the page's valid-token count
+            _lib.call("akv_append_rows", k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2), 1,
+                      take, position, self.table.data_ptr(), self.capacity, page,
+                      None if fresh is None else fresh.data_ptr(), self.pool.arena.data_ptr(), self.pool.nbytes,
+                      self.heads, self.dim, _lib.status_ptr(dev), _lib.stream_of(dev))
             self.length += take
             offset += take
-            self._publish(page)
             self._archive_old_pages()
 
     def _archive_old_pages(self):
@@ -233,8 +234,7 @@ class PagedLayer:
             dst.append(encode(bits, ntok, new))
             self._slots[page] = (bits, new)
         dev = self.device
-        src_t = torch.tensor(src, dtype=torch.int64).to(dev, non_blocking=False)
-        dst_t = torch.tensor(dst, dtype=torch.int64).to(dev, non_blocking=False)
+        src_t, dst_t = to_device(src, dev), to_device(dst, dev)  # pinned, non-blocking: no host stall
         _lib.call("akv_repack_pages", src_t.data_ptr(), dst_t.data_ptr(), len(pages),
                   self.pool.arena.data_ptr(), self.pool.nbytes, self.heads, self.dim, self.group,
                   _lib.SEM_PAGE, _lib.status_ptr(dev), _lib.stream_of(dev))
@@ -242,8 +242,9 @@ class PagedLayer:
             old_bits = {1: 4, 2: 8, 3: 16}[d & 3]
             self.pool.free(old_bits, d >> 8)  # stream order: later writes follow the repack
             self.pages[page] = self._views(*self._slots[page])
-            self._publish(page)
             self.demotions += 1
+        # the new descriptors, written on the device after the repack (no host-built index)
+        self.table.index_copy_(0, to_device(pages, dev), dst_t)
 
     def protect(self, page):
         if page < len(self.pages) and self.pages[page][0].bits != 16:

@@ -98,6 +98,21 @@ def decode(desc: int) -> tuple[int | None, int, int]:
     return (MODE_TO_BITS.get(mode), ((desc >> 2) & 15) + 1, desc >> 8)
 
 
+def to_device(array, device) -> torch.Tensor:
+    """An int64 host array on ``device`` through pinned memory, without blocking
+    the host (torch keeps the pinned block until the copy has run)."""
+    return torch.from_numpy(np.ascontiguousarray(array, np.int64)).pin_memory().to(device, non_blocking=True)
+
+
+def as_fp16_rows(t: torch.Tensor) -> torch.Tensor:
+    """``t`` as fp16 with head_dim contiguous, 8-byte aligned rows and strides in
+    whole 4-element units (the layout akv_append_rows reads)."""
+    t = t.to(torch.float16)
+    if t.stride(-1) != 1 or t.data_ptr() % 8 or any(s % 4 for s in t.stride()[:-1]):
+        t = t.contiguous()
+    return t
+
+
 def group_ok(dim: int, group: int) -> bool:
     return group in (32, 64, 128, BLOCK * dim)
 

@@ -466,22 +466,26 @@ __global__ void __launch_bounds__(256) append_rows_kernel(
   const int lane = threadIdx.x & 31;
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  const int64_t items = (int64_t)batch * heads * kBlock * 2;
+  // A fresh page has all of its 16 rows written (the new tokens, zeros
+  // elsewhere); an existing page only the new rows.
+  const int span = new_desc ? kBlock : rows;
+  const int row0 = new_desc ? 0 : first_row;
+  const int64_t items = (int64_t)batch * heads * span * 2;
   for (int64_t it = warp; it < items; it += nwarps) {
     const int kv = (int)(it & 1);
-    const int r = (int)((it >> 1) % kBlock);
-    const int h = (int)((it >> 1) / kBlock % heads);
-    const int b = (int)((it >> 1) / kBlock / heads);
+    const int r = row0 + (int)((it >> 1) % span);
+    const int h = (int)((it >> 1) / span % heads);
+    const int b = (int)((it >> 1) / span / heads);
     int64_t *entry = table + (int64_t)b * table_stride + page;
     const int64_t d = new_desc ? new_desc[b] : *entry;
+    const bool lead = h == 0 && r == row0 && kv == 0;  // one warp per sequence
     if (desc_mode(d) != AKV_MODE_FP16 || !page_in_arena(d, RB * heads, arena_bytes)) {
-      if (lane == 0 && h == 0 && r == 0 && kv == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+      if (lane == 0 && lead) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
       continue;
     }
-    if (lane == 0 && h == 0 && r == 0 && kv == 0)  // one warp per sequence publishes the new count
+    if (lane == 0 && lead)  // publish the new valid-token count (mode and offset unchanged)
       *entry = (d & ~((int64_t)15 << 2)) | ((int64_t)(first_row + rows - 1) << 2);
     const bool written = r >= first_row && r < first_row + rows;
-    if (!written && !new_desc) continue;
     uint8_t *pay = arena + desc_offset(d) + h * RB + kv * (kBlock * D * 2);
     if (lane < LANES) {
       uint2 v = make_uint2(0u, 0u);
@@ -700,7 +704,7 @@ extern "C" int akv_append_rows(const void *src_k, const void *src_v, int64_t src
   if (rows <= 0 || first_row < 0 || first_row + rows > kBlock || table_stride <= page) return AKV_ERR_INVALID;
   if (((uintptr_t)src_k & 7) || ((uintptr_t)src_v & 7) || !aligned16(arena)) return AKV_ERR_INVALID;
   if (src_batch_stride % 4 || src_head_stride % 4 || src_token_stride % 4) return AKV_ERR_INVALID;
-  const int grid = grid_for((int64_t)batch * heads * kBlock * 2);
+  const int grid = grid_for((int64_t)batch * heads * (new_desc ? kBlock : rows) * 2);
   cudaStream_t s = (cudaStream_t)stream;
 #define AKV_APPEND(D)                                                                                     \
   append_rows_kernel<D><<<grid, 256, 0, s>>>((const __half *)src_k, (const __half *)src_v, src_batch_stride, \
