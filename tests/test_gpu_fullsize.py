@@ -12,9 +12,11 @@ Two size-independent checks:
   blocks, agrees with both).
 
 Geometries: one layer of the batched workload (64 sequences x 8192 tokens, 16 query / 8 KV heads,
-head_dim 128, pages 15/35/40/10 % FP16/INT8/INT4/evicted) and one 1,048,576-token sequence (32 query
-/ 8 KV heads, 5/25/70 % FP16/INT8/INT4), one fp16 scale per (page, KV head) as in the benchmark, K and
-V N(0, 1) with 4 outlier channels per (sequence, head) scaled by 8."""
+head_dim 128, pages 15/35/40/10 % FP16/INT8/INT4/evicted), one 1,048,576-token sequence (32 query
+/ 8 KV heads, 5/25/70 % FP16/INT8/INT4) and one layer of the large-batch workload (128 sequences x
+32,768 tokens, 32 query / 8 KV heads, 5 % evicted, the rest 10/20/70 % FP16/INT8/INT4), one fp16 scale
+per (page, KV head) as in the benchmark, K and V N(0, 1) with 4 outlier channels per (sequence, head)
+scaled by 8."""
 
 import math
 
@@ -31,6 +33,9 @@ ATOL, RTOL = 2e-3, 1e-2
 D = 128
 BATCHED = dict(batch=64, kv_heads=8, q_heads=16, tokens=8192, mix={16: .15, 8: .35, 4: .40, 0: .10})
 LONG = dict(batch=1, kv_heads=8, q_heads=32, tokens=1 << 20, mix={16: .05, 8: .25, 4: .70})
+# One layer of the large-batch workload: GQA 4, 128 sequences x 32,768 tokens, 5 % of pages evicted
+# and the rest 10/20/70 % FP16/INT8/INT4.
+LARGE = dict(batch=128, kv_heads=8, q_heads=32, tokens=32768, mix={16: .095, 8: .19, 4: .665, 0: .05})
 
 
 def _kv(gen, shape, device):
@@ -85,7 +90,8 @@ def _reference(store, q, scale, chunk):
     return torch.cat(out)
 
 
-@pytest.mark.parametrize("geometry,splits,chunk", [(BATCHED, 8, 16), (LONG, 0, 1)], ids=["batched", "long"])
+@pytest.mark.parametrize("geometry,splits,chunk", [(BATCHED, 8, 16), (LONG, 0, 1), (LARGE, 8, 4)],
+                         ids=["batched", "long", "large"])
 def test_full_size_decode_against_float32_attention(cuda, geometry, splits, chunk):
     store = _store(cuda, 90 + splits, **geometry)
     gen = torch.Generator(device=cuda).manual_seed(7)
