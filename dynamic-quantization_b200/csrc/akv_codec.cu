@@ -73,6 +73,100 @@ __global__ void __launch_bounds__(256) dequantize_flat_kernel(const uint8_t *__r
   }
 }
 
+// Vector path for the common shapes: groups of G = 8 * L elements (L a power
+// of two, 1..32) over a whole number of groups.  Thread t owns elements
+// 8t .. 8t + 7 (one 16-byte load of fp16/bf16, two of fp32); the L lanes of a
+// group are adjacent in a warp, so the group absmax is a shuffle reduction.
+// Same arithmetic as quantize_flat_kernel: IEEE division per element.
+template <typename T>
+__device__ __forceinline__ void load8(const T *p, float (&x)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = *reinterpret_cast<const float4 *>(p), b = *reinterpret_cast<const float4 *>(p + 4);
+    x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+  } else {
+    const uint4 w = *reinterpret_cast<const uint4 *>(p);
+    const T *h = reinterpret_cast<const T *>(&w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = to_f32<T>(h[i]);
+  }
+}
+
+template <typename T, int BITS, int SEM>
+__global__ void __launch_bounds__(256) quantize_vec_kernel(const T *__restrict__ src, int64_t nthreads, int lanes,
+                                                           uint8_t *__restrict__ payload, __half *__restrict__ scales) {
+  const float qmax = BITS == 8 ? 127.f : 7.f;
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) & ~(int64_t)31; t0 < nthreads; t0 += stride) {
+    const int64_t t = t0 + lane;
+    const bool active = t < nthreads;  // inactive lanes form whole groups (nthreads is a multiple of lanes)
+    float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (active) load8<T>(src + 8 * t, x);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (SEM == AKV_SEM_PAGE) x[i] = __half2float(__float2half_rn(x[i]));  // pack_page rounds to fp16 first
+      amax = fmaxf(amax, fabsf(x[i]));
+    }
+    for (int off = 1; off < lanes; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (!active) continue;
+    const GroupScale g = group_scale<SEM>(amax, qmax);
+    int q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = quantize_value(x[i], g.divisor, qmax);
+    if (BITS == 8) {
+      uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w0 |= (uint32_t)(q[i] & 255) << (8 * i), w1 |= (uint32_t)(q[4 + i] & 255) << (8 * i);
+      *reinterpret_cast<uint2 *>(payload + 8 * t) = make_uint2(w0, w1);
+    } else {
+      uint32_t w = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w |= (uint32_t)(q[i] & 15) << (4 * i);
+      *reinterpret_cast<uint32_t *>(payload + 4 * t) = w;
+    }
+    if ((t & (lanes - 1)) == 0) scales[t / lanes] = g.stored;
+  }
+}
+
+// Dequantize 8 elements per thread (group a multiple of 8: one scale each).
+template <typename T, int BITS>
+__global__ void __launch_bounds__(256) dequantize_vec_kernel(const uint8_t *__restrict__ payload,
+                                                             const __half *__restrict__ scales, int64_t nthreads,
+                                                             int64_t group8, T *__restrict__ out) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < nthreads; t += stride) {
+    const float s = __half2float(scales[t / group8]);
+    float y[8];
+    if (BITS == 8) {
+      const uint2 w = *reinterpret_cast<const uint2 *>(payload + 8 * t);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        y[i] = (float)(int)(int8_t)(w.x >> (8 * i)) * s;
+        y[4 + i] = (float)(int)(int8_t)(w.y >> (8 * i)) * s;
+      }
+    } else {
+      const uint32_t w = *reinterpret_cast<const uint32_t *>(payload + 4 * t);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int n = (w >> (4 * i)) & 15;
+        y[i] = (float)(n >= 8 ? n - 16 : n) * s;  // sign extension (backend.py:172)
+      }
+    }
+    if constexpr (sizeof(T) == 4) {
+      float4 *o = reinterpret_cast<float4 *>(out + 8 * t);
+      o[0] = make_float4(y[0], y[1], y[2], y[3]);
+      o[1] = make_float4(y[4], y[5], y[6], y[7]);
+    } else {
+      uint4 w;
+      T *h = reinterpret_cast<T *>(&w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = from_f32<T>(y[i]);
+      *reinterpret_cast<uint4 *>(out + 8 * t) = w;
+    }
+  }
+}
+
 // ============================================================ page records
 // A slab is one (page, head, K-or-V) 16 x D fp16 tile.  Lane l of the warp owns
 // elements 256*c + 8*l + [0, 8) for chunk c < D/16: one 16-byte fp16 vector per
@@ -598,8 +692,34 @@ extern "C" int akv_quantize(const void *src, int src_dtype, int64_t numel, int64
   if (bits == 4 && group % 2) return AKV_ERR_INVALID;
   if (semantics != AKV_SEM_TENSOR && semantics != AKV_SEM_PAGE) return AKV_ERR_INVALID;
   const int64_t ngroups = (numel + group - 1) / group;
-  const int grid = grid_for(ngroups);
   cudaStream_t s = (cudaStream_t)stream;
+  // Vector path: a power-of-two group of 8..256 elements, whole groups,
+  // 16-byte aligned source and naturally aligned payload.
+  const bool pow2 = (group & (group - 1)) == 0;
+  if (pow2 && group >= 8 && group <= 256 && numel % group == 0 && ((uintptr_t)src & 15) == 0 &&
+      ((uintptr_t)payload & (bits == 8 ? 7 : 3)) == 0) {
+    const int64_t nthreads = numel / 8;
+    const int lanes = (int)(group / 8);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nthreads + 255) / 256, 148ll * 64));
+#define AKV_QV(T, B, S)                                                                                  \
+  quantize_vec_kernel<T, B, S><<<grid, 256, 0, s>>>((const T *)src, nthreads, lanes, (uint8_t *)payload, \
+                                                    (__half *)scales)
+#define AKV_QVB(T, S) \
+  if (bits == 8) AKV_QV(T, 8, S); else AKV_QV(T, 4, S)
+#define AKV_QVS(T) \
+  if (semantics == AKV_SEM_TENSOR) { AKV_QVB(T, AKV_SEM_TENSOR); } else { AKV_QVB(T, AKV_SEM_PAGE); }
+    switch (src_dtype) {
+      case AKV_DTYPE_F32: AKV_QVS(float); break;
+      case AKV_DTYPE_F16: AKV_QVS(__half); break;
+      case AKV_DTYPE_BF16: AKV_QVS(__nv_bfloat16); break;
+      default: return AKV_ERR_INVALID;
+    }
+#undef AKV_QVS
+#undef AKV_QVB
+#undef AKV_QV
+    return launch_status();
+  }
+  const int grid = grid_for(ngroups);
 #define AKV_Q(T, B, S)                                                                   \
   quantize_flat_kernel<T, B, S><<<grid, 256, 0, s>>>((const T *)src, numel, group, ngroups, \
                                                        (uint8_t *)payload, (__half *)scales)
@@ -623,8 +743,28 @@ extern "C" int akv_dequantize(const void *payload, const void *scales, int64_t n
                               int bits, void *out, int out_dtype, void *stream) {
   if (!payload || !scales || !out || numel <= 0 || group <= 0) return AKV_ERR_INVALID;
   if (bits != 4 && bits != 8) return AKV_ERR_INVALID;
-  const int grid = grid_for((numel + 31) / 32);
   cudaStream_t s = (cudaStream_t)stream;
+  if (group % 8 == 0 && numel % 8 == 0 && ((uintptr_t)out & 15) == 0 &&
+      ((uintptr_t)payload & (bits == 8 ? 7 : 3)) == 0) {  // vector path: 8 elements (one scale) per thread
+    const int64_t nthreads = numel / 8;
+    const int vgrid = (int)std::max<int64_t>(1, std::min<int64_t>((nthreads + 255) / 256, 148ll * 64));
+#define AKV_DV(T)                                                                                              \
+  if (bits == 8)                                                                                               \
+    dequantize_vec_kernel<T, 8><<<vgrid, 256, 0, s>>>((const uint8_t *)payload, (const __half *)scales, nthreads, \
+                                                      group / 8, (T *)out);                                     \
+  else                                                                                                         \
+    dequantize_vec_kernel<T, 4><<<vgrid, 256, 0, s>>>((const uint8_t *)payload, (const __half *)scales, nthreads, \
+                                                      group / 8, (T *)out)
+    switch (out_dtype) {
+      case AKV_DTYPE_F32: AKV_DV(float); break;
+      case AKV_DTYPE_F16: AKV_DV(__half); break;
+      case AKV_DTYPE_BF16: AKV_DV(__nv_bfloat16); break;
+      default: return AKV_ERR_INVALID;
+    }
+#undef AKV_DV
+    return launch_status();
+  }
+  const int grid = grid_for((numel + 31) / 32);
 #define AKV_D(T)                                                                           \
   if (bits == 8)                                                                           \
     dequantize_flat_kernel<T, 8><<<grid, 256, 0, s>>>((const uint8_t *)payload,            \
