@@ -73,100 +73,6 @@ __global__ void __launch_bounds__(256) dequantize_flat_kernel(const uint8_t *__r
   }
 }
 
-// Vector path for the common shapes: groups of G = 8 * L elements (L a power
-// of two, 1..32) over a whole number of groups.  Thread t owns elements
-// 8t .. 8t + 7 (one 16-byte load of fp16/bf16, two of fp32); the L lanes of a
-// group are adjacent in a warp, so the group absmax is a shuffle reduction.
-// Same arithmetic as quantize_flat_kernel: IEEE division per element.
-template <typename T>
-__device__ __forceinline__ void load8(const T *p, float (&x)[8]) {
-  if constexpr (sizeof(T) == 4) {
-    const float4 a = *reinterpret_cast<const float4 *>(p), b = *reinterpret_cast<const float4 *>(p + 4);
-    x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
-  } else {
-    const uint4 w = *reinterpret_cast<const uint4 *>(p);
-    const T *h = reinterpret_cast<const T *>(&w);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = to_f32<T>(h[i]);
-  }
-}
-
-template <typename T, int BITS, int SEM>
-__global__ void __launch_bounds__(256) quantize_vec_kernel(const T *__restrict__ src, int64_t nthreads, int lanes,
-                                                           uint8_t *__restrict__ payload, __half *__restrict__ scales) {
-  const float qmax = BITS == 8 ? 127.f : 7.f;
-  const int lane = threadIdx.x & 31;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t t0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) & ~(int64_t)31; t0 < nthreads; t0 += stride) {
-    const int64_t t = t0 + lane;
-    const bool active = t < nthreads;  // inactive lanes form whole groups (nthreads is a multiple of lanes)
-    float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (active) load8<T>(src + 8 * t, x);
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (SEM == AKV_SEM_PAGE) x[i] = __half2float(__float2half_rn(x[i]));  // pack_page rounds to fp16 first
-      amax = fmaxf(amax, fabsf(x[i]));
-    }
-    for (int off = 1; off < lanes; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    if (!active) continue;
-    const GroupScale g = group_scale<SEM>(amax, qmax);
-    int q[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = quantize_value(x[i], g.divisor, qmax);
-    if (BITS == 8) {
-      uint32_t w0 = 0, w1 = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) w0 |= (uint32_t)(q[i] & 255) << (8 * i), w1 |= (uint32_t)(q[4 + i] & 255) << (8 * i);
-      *reinterpret_cast<uint2 *>(payload + 8 * t) = make_uint2(w0, w1);
-    } else {
-      uint32_t w = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) w |= (uint32_t)(q[i] & 15) << (4 * i);
-      *reinterpret_cast<uint32_t *>(payload + 4 * t) = w;
-    }
-    if ((t & (lanes - 1)) == 0) scales[t / lanes] = g.stored;
-  }
-}
-
-// Dequantize 8 elements per thread (group a multiple of 8: one scale each).
-template <typename T, int BITS>
-__global__ void __launch_bounds__(256) dequantize_vec_kernel(const uint8_t *__restrict__ payload,
-                                                             const __half *__restrict__ scales, int64_t nthreads,
-                                                             int64_t group8, T *__restrict__ out) {
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < nthreads; t += stride) {
-    const float s = __half2float(scales[t / group8]);
-    float y[8];
-    if (BITS == 8) {
-      const uint2 w = *reinterpret_cast<const uint2 *>(payload + 8 * t);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        y[i] = (float)(int)(int8_t)(w.x >> (8 * i)) * s;
-        y[4 + i] = (float)(int)(int8_t)(w.y >> (8 * i)) * s;
-      }
-    } else {
-      const uint32_t w = *reinterpret_cast<const uint32_t *>(payload + 4 * t);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int n = (w >> (4 * i)) & 15;
-        y[i] = (float)(n >= 8 ? n - 16 : n) * s;  // sign extension (backend.py:172)
-      }
-    }
-    if constexpr (sizeof(T) == 4) {
-      float4 *o = reinterpret_cast<float4 *>(out + 8 * t);
-      o[0] = make_float4(y[0], y[1], y[2], y[3]);
-      o[1] = make_float4(y[4], y[5], y[6], y[7]);
-    } else {
-      uint4 w;
-      T *h = reinterpret_cast<T *>(&w);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) h[i] = from_f32<T>(y[i]);
-      *reinterpret_cast<uint4 *>(out + 8 * t) = w;
-    }
-  }
-}
-
 // ============================================================ page records
 // A slab is one (page, head, K-or-V) 16 x D fp16 tile.  Lane l of the warp owns
 // elements 256*c + 8*l + [0, 8) for chunk c < D/16: one 16-byte fp16 vector per
@@ -406,6 +312,121 @@ __device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], i
           prmt(prmt(pb[0], pb[1], 0x0040u), prmt(pb[2], pb[3], 0x0040u), 0x5410u);
     }
     if (e % G == 0) sc[e / G] = gs.stored;
+  }
+}
+
+// Vector path for the common shapes: groups of G = 8 * L elements (L a power
+// of two, 1..32) over a whole number of groups.  Thread t owns elements
+// 8t .. 8t + 7 (one 16-byte load of fp16/bf16, two of fp32); the L lanes of a
+// group are adjacent in a warp, so the group absmax is a shuffle reduction.
+// Same arithmetic as quantize_flat_kernel: IEEE division per element.
+template <typename T>
+__device__ __forceinline__ void load8(const T *p, float (&x)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = *reinterpret_cast<const float4 *>(p), b = *reinterpret_cast<const float4 *>(p + 4);
+    x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+  } else {
+    const uint4 w = *reinterpret_cast<const uint4 *>(p);
+    const T *h = reinterpret_cast<const T *>(&w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = to_f32<T>(h[i]);
+  }
+}
+
+// Thread t's 8 integers (two's complement in their low bits) as payload bytes:
+// INT8 one byte each, INT4 two per byte with the even element low.
+template <int BITS>
+__device__ __forceinline__ void store_quantized(const uint32_t (&q)[8], uint8_t *payload, int64_t t) {
+  if (BITS == 8) {
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w0 |= (q[i] & 255u) << (8 * i), w1 |= (q[4 + i] & 255u) << (8 * i);
+    *reinterpret_cast<uint2 *>(payload + 8 * t) = make_uint2(w0, w1);
+  } else {
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w |= (q[i] & 15u) << (4 * i);
+    *reinterpret_cast<uint32_t *>(payload + 4 * t) = w;
+  }
+}
+
+template <typename T, int BITS, int SEM>
+__global__ void __launch_bounds__(256) quantize_vec_kernel(const T *__restrict__ src, int64_t nthreads, int lanes,
+                                                           uint8_t *__restrict__ payload, __half *__restrict__ scales) {
+  const float qmax = BITS == 8 ? 127.f : 7.f;
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t0 = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) & ~(int64_t)31; t0 < nthreads; t0 += stride) {
+    const int64_t t = t0 + lane;
+    const bool active = t < nthreads;  // inactive lanes form whole groups (nthreads is a multiple of lanes)
+    if constexpr (std::is_same<T, __half>::value) {
+      // fp16 values: absmax in the fp16 domain and the exact reciprocal-multiply
+      // rounding with its tie fallback (quantize_chunk), warp-collective
+      const uint4 raw = active ? *reinterpret_cast<const uint4 *>(src + 8 * t) : make_uint4(0, 0, 0, 0);
+      float amax = chunk_absmax(raw);
+      for (int off = 1; off < lanes; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      const GroupScale g = group_scale<SEM>(amax, qmax);
+      uint32_t q[8];
+      quantize_chunk(raw, g.divisor, __frcp_rn(g.divisor), qmax, q);
+      if (!active) continue;
+      store_quantized<BITS>(q, payload, t);
+      if ((t & (lanes - 1)) == 0) scales[t / lanes] = g.stored;
+      continue;
+    }
+    float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (active) load8<T>(src + 8 * t, x);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (SEM == AKV_SEM_PAGE) x[i] = __half2float(__float2half_rn(x[i]));  // pack_page rounds to fp16 first
+      amax = fmaxf(amax, fabsf(x[i]));
+    }
+    for (int off = 1; off < lanes; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (!active) continue;
+    const GroupScale g = group_scale<SEM>(amax, qmax);
+    uint32_t q[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q[i] = (uint32_t)quantize_value(x[i], g.divisor, qmax);
+    store_quantized<BITS>(q, payload, t);
+    if ((t & (lanes - 1)) == 0) scales[t / lanes] = g.stored;
+  }
+}
+
+// Dequantize 8 elements per thread (group a multiple of 8: one scale each).
+template <typename T, int BITS>
+__global__ void __launch_bounds__(256) dequantize_vec_kernel(const uint8_t *__restrict__ payload,
+                                                             const __half *__restrict__ scales, int64_t nthreads,
+                                                             int64_t group8, T *__restrict__ out) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < nthreads; t += stride) {
+    const float s = __half2float(scales[t / group8]);
+    float y[8];
+    if (BITS == 8) {
+      const uint2 w = *reinterpret_cast<const uint2 *>(payload + 8 * t);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        y[i] = (float)(int)(int8_t)(w.x >> (8 * i)) * s;
+        y[4 + i] = (float)(int)(int8_t)(w.y >> (8 * i)) * s;
+      }
+    } else {
+      const uint32_t w = *reinterpret_cast<const uint32_t *>(payload + 4 * t);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int n = (w >> (4 * i)) & 15;
+        y[i] = (float)(n >= 8 ? n - 16 : n) * s;  // sign extension (backend.py:172)
+      }
+    }
+    if constexpr (sizeof(T) == 4) {
+      float4 *o = reinterpret_cast<float4 *>(out + 8 * t);
+      o[0] = make_float4(y[0], y[1], y[2], y[3]);
+      o[1] = make_float4(y[4], y[5], y[6], y[7]);
+    } else {
+      uint4 w;
+      T *h = reinterpret_cast<T *>(&w);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = from_f32<T>(y[i]);
+      *reinterpret_cast<uint4 *>(out + 8 * t) = w;
+    }
   }
 }
 
