@@ -980,37 +980,29 @@ __global__ void __launch_bounds__(1024) merge_wide_kernel(const int32_t *__restr
 // ======================================== cross-GPU merge over peer memory
 // One long sequence split over `world` GPUs: every rank decodes its page range
 // into partial states, then this kernel, per (sequence, query head) row,
-// (1) merges a share of the rank's partials into one state: kExchangeSplit
-//     CTAs per row, each folding every kExchangeSplit-th group of 32
-//     contributors (a long sequence has ~300 per row, so one CTA per row left
-//     most SMs idle while 32 of them folded serially),
+// (1) merges the rank's partials into one state (as merge_wide_kernel),
 // (2) stores that state into every rank's exchange buffer over NVLink (plain
-//     peer stores) and raises its flag there with a system-scope release,
-// (3) the last of the row's CTAs on this GPU to publish (an atomic ticket, so
-//     no CTA waits on a sibling that might not be running) waits (bounded)
-//     until every rank's flags of the row carry this call's epoch, and
-// (4) merges the world's states into the output.
-// A row's wait depends only on CTAs that publish before they wait or never
-// wait, so no CTA waits on one that cannot run.
+//     peer stores) and raises the row's flag there with a system-scope release,
+// (3) waits (bounded) until every rank's flag for the row carries this call's
+//     epoch, and (4) merges the world's states into the output.
+// A row's wait depends only on the same row's CTA on the other GPUs, which
+// stores before it waits, so no CTA waits on one that cannot run.
 //
 // Exchange buffer of one rank (akv_exchange_bytes): fp32 states
-// [2][world][kExchangeSplit][rows][D+2] (slot [e & 1][r][s] holds share s of
-// rank r's state of every row for the calls of epoch parity e & 1), then uint32
-// flags of the same shape (the epoch of the last call of that parity whose
-// share landed), then uint32 tickets [rows].  Buffers start zeroed; epochs
-// start at 1.
+// [2][world][rows][D+2] (slot [e & 1][r] holds rank r's state of every row for
+// the calls of epoch parity e & 1), then uint32 flags [2][world][rows] (flag
+// [e & 1][r][row] = the epoch of the last call of that parity whose rank-r
+// state of the row has landed).  Buffers start zeroed; epochs start at 1.
 //
 // Two parities make consecutive calls safe without any extra handshake: rank
 // A's call e + 2 writes the parity-(e & 1) slots again only after its call
-// e + 1 finished, which needed every peer's call-(e + 1) states of every row,
+// e + 1 finished, which needed every peer's call-(e + 1) state of every row,
 // and a peer publishes e + 1 only after its whole call-e grid (every read of
 // the parity-(e & 1) slots) has completed: its decode of e + 1 waits for that
 // grid, and its exchange of e + 1 waits for the decode.  With one slot a fast
 // rank's call e + 1 could overwrite a state (and move the flag past e) that a
 // slower rank was still waiting for or reading.
 constexpr int kMaxPeers = 8;
-constexpr int kExchangeSplit = 4;  // CTAs per row; world * kExchangeSplit flags fit one warp
-static_assert(kMaxPeers * kExchangeSplit <= 32, "one lane watches one flag");
 struct PeerBuffers {
   void *buf[kMaxPeers];
 };
@@ -1029,27 +1021,26 @@ __global__ void __launch_bounds__(1024) merge_exchange_kernel(const int32_t *__r
                                                               PeerBuffers peers, int rank, int world,
                                                               uint32_t epoch, __half *__restrict__ out,
                                                               int64_t obs, int64_t ohs, int32_t *status) {
-  constexpr int VEC = D / 32, W = 32, RS = D + 2, S = kExchangeSplit;
+  constexpr int PS = D + 4, VEC = D / 32, W = 32, RS = D + 2;
   __shared__ float sm_acc[W][D];
   __shared__ float sm_m[W], sm_l[W];
   grid_dependency_wait();
   MergeGeom g;
   if (!merge_geom<D>(header, g)) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
-      set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
     return;
   }
-  const int h = blockIdx.x, b = blockIdx.y, share = blockIdx.z;
+  const int h = blockIdx.x, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = h / g.gqa, r = h - kvh * g.gqa, qg = r >> 3, n = r & 7;
   const int item = (b * g.kv_heads + kvh) * g.qgroups + qg;
   float m = -INFINITY, l = 0.f, acc[VEC];
 #pragma unroll
   for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
-  if (g.mb > 0) {  // (1) this CTA's share: warp w folds contributors w, w + 32 * S, ... of its group
+  if (g.mb > 0) {  // (1) this rank's partials, warp w folding contributors w, w + 32, ...
     const int w0 = item * g.mb / g.range;
-    fold_partials<D>(g, item, n, w0 + share * W + warp, min(((item + 1) * g.mb - 1) / g.range, g.warps - 1),
-                     W * S, lane, m, l, acc);
+    fold_partials<D>(g, item, n, w0 + warp, min(((item + 1) * g.mb - 1) / g.range, g.warps - 1), W, lane, m, l,
+                     acc);
   }
 #pragma unroll
   for (int i = 0; i < VEC; ++i) sm_acc[warp][VEC * lane + i] = acc[i];
@@ -1071,37 +1062,29 @@ __global__ void __launch_bounds__(1024) merge_exchange_kernel(const int32_t *__r
   }
   const int rows = gridDim.x * gridDim.y, row = b * q_heads + h;
   const int64_t par = epoch & 1u;
-  const int64_t slots = 2ll * world * S * rows;  // states (and flags) per buffer, both parities
-  auto state_at = [&](void *buf, int64_t src, int64_t sh) {
-    return reinterpret_cast<float *>(buf) + (((par * world + src) * S + sh) * rows + row) * RS;
-  };
-  auto flag_at = [&](void *buf, int64_t src, int64_t sh) {
-    return reinterpret_cast<uint32_t *>(reinterpret_cast<float *>(buf) + slots * RS) +
-           ((par * world + src) * S + sh) * rows + row;
-  };
-  // (2) publish this share to every rank, this one included, into this epoch parity's slots
+  const int64_t flag_offset = 2ll * world * rows * RS;  // in floats: the flags follow both parities' states
+  // (2) publish to every rank, this one included, into this epoch parity's slots
   for (int pr = 0; pr < world; ++pr) {
-    float *st = state_at(peers.buf[pr], rank, share);
+    float *st = reinterpret_cast<float *>(peers.buf[pr]) + ((par * world + rank) * rows + row) * RS;
 #pragma unroll
     for (int i = 0; i < VEC; ++i) st[VEC * lane + i] = num[i];
     if (lane == 0) st[D] = top, st[D + 1] = den;
   }
   __threadfence_system();  // each lane's state stores before any flag
   __syncwarp();
-  if (lane < world) st_release_sys(flag_at(peers.buf[lane], rank, share), epoch);
-  // (3) the row's last CTA on this GPU to publish goes on; the others are done
-  uint32_t *tickets = reinterpret_cast<uint32_t *>(reinterpret_cast<float *>(peers.buf[rank]) + slots * RS) + slots;
-  uint32_t ticket = 0;
-  if (lane == 0) ticket = atomicAdd(tickets + row, 1u);
-  ticket = __shfl_sync(0xffffffffu, ticket, 0);
-  if (ticket != S - 1) return;
-  if (lane == 0) tickets[row] = 0;  // the next call on this buffer runs after this grid: it starts from zero
-  // bounded wait for every rank's every share of this row (lane q * S + s watches share s of rank q)
+  if (lane < world)
+    st_release_sys(reinterpret_cast<uint32_t *>(reinterpret_cast<float *>(peers.buf[lane]) + flag_offset) +
+                       (par * world + rank) * rows + row,
+                   epoch);
+  // (3) bounded wait for every rank's state of this row (lane q watches rank q)
+  const float *mine = reinterpret_cast<const float *>(peers.buf[rank]) + par * world * rows * RS;
+  const uint32_t *flags =
+      reinterpret_cast<const uint32_t *>(reinterpret_cast<const float *>(peers.buf[rank]) + flag_offset) +
+      par * world * rows;
   bool ok = true;
-  if (lane < world * S) {
-    const uint32_t *f = flag_at(peers.buf[rank], lane / S, lane % S);
+  if (lane < world) {
     const uint64_t t0 = globaltimer();
-    while (ld_acquire_sys(f) != epoch)
+    while (ld_acquire_sys(flags + (int64_t)lane * rows + row) != epoch)
       if (globaltimer() - t0 > kWaitNs) {
         ok = false;
         break;
@@ -1115,9 +1098,9 @@ __global__ void __launch_bounds__(1024) merge_exchange_kernel(const int32_t *__r
   float mt = -INFINITY, lt = 0.f, at[VEC];
 #pragma unroll
   for (int i = 0; i < VEC; ++i) at[i] = 0.f;
-  for (int k = 0; k < world * S; ++k) {
-    (void)ld_acquire_sys(flag_at(peers.buf[rank], k / S, k % S));
-    const float *st = state_at(peers.buf[rank], k / S, k % S);
+  for (int q = 0; q < world; ++q) {
+    (void)ld_acquire_sys(flags + (int64_t)q * rows + row);
+    const float *st = mine + ((int64_t)q * rows + row) * RS;
     const float mq = __ldcg(st + D), lq = __ldcg(st + D + 1);
     if (mq == -INFINITY) continue;
     const float tp = fmaxf(mt, mq), c = ex2(mt - tp), e = ex2(mq - tp);
@@ -1379,8 +1362,8 @@ extern "C" int akv_merge(const void *workspace, int32_t batch, int32_t q_heads, 
 extern "C" int64_t akv_exchange_bytes(int32_t world, int32_t batch, int32_t q_heads, int32_t head_dim) {
   if (world <= 0 || world > kMaxPeers || batch <= 0 || q_heads <= 0 || (head_dim != 64 && head_dim != 128))
     return -1;
-  const int64_t rows = (int64_t)batch * q_heads, slots = 2ll * world * kExchangeSplit * rows;
-  return (slots * (head_dim + 2) * 4 + slots * 4 + rows * 4 + 15) & ~15ll;  // states, flags, tickets
+  const int64_t rows = (int64_t)batch * q_heads;
+  return 2 * (world * rows * (head_dim + 2) * 4 + world * rows * 4);  // both epoch parities
 }
 
 extern "C" int akv_merge_exchange(const void *workspace, int32_t batch, int32_t q_heads, int32_t head_dim,
@@ -1397,7 +1380,7 @@ extern "C" int akv_merge_exchange(const void *workspace, int32_t batch, int32_t 
   }
   const int32_t *header = (const int32_t *)workspace;
   cudaStream_t s = (cudaStream_t)stream;
-  const dim3 grid(q_heads, batch, kExchangeSplit);
+  const dim3 grid(q_heads, batch);
   const cudaError_t err =
       head_dim == 64 ? launch_dependent(merge_exchange_kernel<64>, grid, 1024, 0, s, header, (int)q_heads, peers,
                                         (int)rank, (int)world, epoch, (__half *)out, out_batch_stride,
