@@ -28,9 +28,8 @@
 //  * a page's K/V are dequantised in registers straight into tensor-core
 //    fragments (exact: the integer is formed in fp16 by an exponent trick and
 //    multiplied by the fp16 scale with one rounding, matching
-//    fp16(int * float(scale)) of packed_decode.py:45 / triton_decode.py:31);
-//    with one scale per page (group = 16 * head_dim) the V scale is instead
-//    multiplied into the page's fp16 P fragment, one rounding per term as well;
+//    fp16(int * float(scale)) of packed_decode.py:45 / triton_decode.py:31),
+//    for K and V alike;
 //  * Q.K^T and P.V run as mma.sync m16n8k16 (f16 x f16 -> f32): 16 tokens x 8
 //    query heads per page, 2 * head_dim/16 MMAs per page;
 //  * the online softmax is fp32 in base 2; the running max only moves (one
@@ -222,8 +221,7 @@ __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, c
 // DV*gid + [0, DV): m-tile m's A rows gid / gid+8 are dims DV*gid + 2m / +2m+1;
 // its k (token) columns 2t4, 2t4+1 / 2t4+8, 2t4+9 match the P fragment that
 // movmatrix produced from the score accumulators.
-// FOLD: the page has a single V scale, already multiplied into P.
-template <int D, int MODE, bool SLAB, bool FOLD>
+template <int D, int MODE, bool SLAB>
 __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, const ScaleIdx &si,
                                         int gid, int t4, uint32_t b0, uint32_t b1,
                                         float (&o)[D / 16][4]) {
@@ -243,9 +241,9 @@ __device__ __forceinline__ void page_pv(const uint8_t *vrec, const __half *vsc, 
   const int c0 = (int)((si.vo >> (MODE == AKV_MODE_INT4 ? 0 : (MODE == AKV_MODE_INT8 ? 10 : 20))) &
                         (MODE == AKV_MODE_FP16 ? 0xfffu : 0x3ffu));
   constexpr int kOddRow = rowB == 64 ? 64 : (rowB == 32 ? 32 : 0);
-  auto sc = [](uint32_t x, uint32_t s) { return FOLD ? x : hmul2(x, s); };
+  auto sc = [](uint32_t x, uint32_t s) { return hmul2(x, s); };  // fp16(int * scale), one rounding
   uint32_t sab = 0, scd = 0;
-  if constexpr (MODE != AKV_MODE_FP16 && !FOLD) {
+  if constexpr (MODE != AKV_MODE_FP16) {
     if constexpr (SLAB) {
       sab = scd = rep_half(vsc);
     } else {
@@ -303,17 +301,16 @@ struct SoftmaxState {
 };
 
 // Online softmax step over one or two pages of one item (fp32, base 2).
-// Returns the fp16 P fragments for P.V, page r's multiplied by ps[r] (its V
-// scale when that is folded into P; the running sums take the unscaled P).
-// Scores are scaled before the max, so any sign of the softmax scale works.
-// The running max moves only when a score exceeds it by more than `slack`
-// (8: P <= 2^8; 0: an exact max, P <= 1).  With NP = 2 the second page is
-// skipped when `two` is false.
+// Returns the fp16 P fragments for P.V.  Scores are scaled before the max, so
+// any sign of the softmax scale works.  The running max moves only when a score
+// exceeds it by more than 2^8 (P <= 2^8 stays exact enough in fp16 and most
+// pages need no reduction).  With NP = 2 the second page is skipped when `two`
+// is false.
 template <int D, int NP>
 __device__ __forceinline__ void pages_softmax(float (&s)[NP][4], const int (&ntok)[NP], bool two,
-                                              int gid, float scale_log2, float slack,
-                                              const float (&ps)[NP], SoftmaxState &st,
+                                              int gid, float scale_log2, SoftmaxState &st,
                                               float (&o)[D / 16][4], uint32_t (&b)[NP][2]) {
+  constexpr float slack = 8.f;
   constexpr float kNegInf = -INFINITY;
   float x[NP][4];
   float mx0 = kNegInf, mx1 = kNegInf;
@@ -348,8 +345,8 @@ __device__ __forceinline__ void pages_softmax(float (&s)[NP][4], const int (&nto
     const float p0 = ex2(x[r][0] - st.m0), p1 = ex2(x[r][1] - st.m1);
     const float p2 = ex2(x[r][2] - st.m0), p3 = ex2(x[r][3] - st.m1);
     st.l0 += p0 + p2, st.l1 += p1 + p3;
-    b[r][0] = movmatrix_trans(pack_f16x2(p0 * ps[r], p1 * ps[r]));
-    b[r][1] = movmatrix_trans(pack_f16x2(p2 * ps[r], p3 * ps[r]));
+    b[r][0] = movmatrix_trans(pack_f16x2(p0, p1));
+    b[r][1] = movmatrix_trans(pack_f16x2(p2, p3));
   }
 }
 
@@ -381,24 +378,22 @@ __device__ __forceinline__ void fp16_attend(uint8_t *rec, int ntok, int lane, co
   float s[1][4];
   uint32_t b[1][2];
   const int nt[1] = {ntok};
-  const float ps[1] = {1.f};
   page_qk<D, AKV_MODE_FP16, SLAB>(rec, nullptr, none, gid, t4, qf, s[0]);
-  pages_softmax<D, 1>(s, nt, false, gid, scale_log2, 8.f, ps, st, o, b);
-  page_pv<D, AKV_MODE_FP16, SLAB, false>(rec + PB, nullptr, si, gid, t4, b[0][0], b[0][1], o);
+  pages_softmax<D, 1>(s, nt, false, gid, scale_log2, st, o, b);
+  page_pv<D, AKV_MODE_FP16, SLAB>(rec + PB, nullptr, si, gid, t4, b[0][0], b[0][1], o);
 }
 
 // A slot of one or two INT8/INT4 pages of one item, adjacent in the ring
 // (`rb` bytes apart), sharing one softmax step.  INT4 pages, the cheapest per
 // instruction, run both pages' Q.K (and P.V) in line, which gives the warp
-// schedulers two independent instruction streams (4 % faster on INT4 pages,
-// 2 % on the mixed layer); INT8 pages share one copy of the code in a
-// two-trip loop, which keeps the kernel's instruction footprint small.
-// With one scale per page (SLAB) each page's V scale is folded into its P
-// fragment: P.V = (P * sV) . v_int, one fp16 rounding per term as in
-// fp16(int * sV).  P <= 2^8 keeps P * sV finite while sV <= 255; a slot with a
-// larger V scale takes an exact running max (P <= 1, so P * sV <= sV).  K keeps
-// the exact per-element fp16(int * sK): the scores would amplify any change
-// through exp.
+// schedulers two independent instruction streams; INT8 pages share one copy of
+// the code in a two-trip loop, which keeps the kernel's instruction footprint
+// small.  K and V are both dequantised exactly as fp16(int * float(scale)), the
+// values the reference attends over: folding V's scale into the fp16 P fragment
+// instead (one rounding of p * sV per term) was 1 % faster on the mixed layer
+// but doubled the error tail of short sequences with outlier channels (66 of
+// 16.7 M outputs beyond 2e-3 of the reference's fp16 SDPA over the same pages,
+// against 0 without it).
 template <int D, int MODE, bool SLAB>
 __device__ __forceinline__ void slot_attend(uint8_t *rec, uint32_t rb, bool has2, int ntok0,
                                             int ntok1, int lane, int log2_group, const ScaleIdx &si,
@@ -431,26 +426,19 @@ __device__ __forceinline__ void slot_attend(uint8_t *rec, uint32_t rb, bool has2
   }
   }
   const int nt[2] = {ntok0, has2 ? ntok1 : 0};
-  float ps[2] = {1.f, 1.f};
-  float slack = 8.f;
-  if constexpr (SLAB) {
-    ps[0] = __half2float(reinterpret_cast<const __half *>(rec + 2 * PB)[vgap]);
-    ps[1] = has2 ? __half2float(reinterpret_cast<const __half *>(rec + rb + 2 * PB)[vgap]) : 0.f;
-    if (!(fmaxf(ps[0], ps[1]) <= 255.f)) slack = 0.f;
-  }
   uint32_t b[2][2];
-  pages_softmax<D, 2>(s, nt, has2, gid, scale_log2, slack, ps, st, o, b);
+  pages_softmax<D, 2>(s, nt, has2, gid, scale_log2, st, o, b);
   if constexpr (MODE == AKV_MODE_INT4) {
-    page_pv<D, MODE, SLAB, SLAB>(rec + PB, reinterpret_cast<const __half *>(rec + 2 * PB) + vgap, si, gid, t4,
+    page_pv<D, MODE, SLAB>(rec + PB, reinterpret_cast<const __half *>(rec + 2 * PB) + vgap, si, gid, t4,
                                  b[0][0], b[0][1], o);
     if (has2)
-      page_pv<D, MODE, SLAB, SLAB>(rec + rb + PB, reinterpret_cast<const __half *>(rec + rb + 2 * PB) + vgap, si,
+      page_pv<D, MODE, SLAB>(rec + rb + PB, reinterpret_cast<const __half *>(rec + rb + 2 * PB) + vgap, si,
                                    gid, t4, b[1][0], b[1][1], o);
   } else {
 #pragma unroll 1
   for (int r = 0; r < npages; ++r) {
     const uint8_t *pg = rec + r * rb;
-    page_pv<D, MODE, SLAB, SLAB>(pg + PB, reinterpret_cast<const __half *>(pg + 2 * PB) + vgap, si, gid, t4,
+    page_pv<D, MODE, SLAB>(pg + PB, reinterpret_cast<const __half *>(pg + 2 * PB) + vgap, si, gid, t4,
                                  r ? b[1][0] : b[0][0], r ? b[1][1] : b[0][1], o);
   }
   }
