@@ -148,8 +148,10 @@ struct ScaleIdx {
 // query heads 2t4, 2t4+1.  The contraction dim is permuted identically in the
 // K (A) and Q (B) fragments: k16 chunk c = 2j + hb takes, from the lane's 8-dim
 // word group j, dims {2hb, 2hb+4} (fragment cols 2t4, 2t4+1) and
-// {2hb+1, 2hb+5} (cols 2t4+8, 2t4+9).  Even and odd chunks accumulate into
-// separate tiles so the MMA dependency chain is half as long.
+// {2hb+1, 2hb+5} (cols 2t4+8, 2t4+9).  All chunks accumulate into one tile:
+// the other page of a slot and the other warps hide the chain's latency, while
+// two tiles cost a register quad and a sum per page (3 % slower on the mixed
+// layer).
 template <int D, int MODE, bool SLAB>
 __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, const ScaleIdx &si,
                                         int gid, int t4, const uint32_t (&qf)[D / 16][2],
@@ -163,7 +165,7 @@ __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, c
   constexpr bool WHOLE = W <= 8;        // narrow slices load at once, wide ones per group
   const uint8_t *row0 = rec + gid * rowB + t4 * (W * 4);
   const uint8_t *row1 = row0 + 8 * rowB;
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
   uint32_t sc0 = 0, sc1 = 0;
   if constexpr (MODE != AKV_MODE_FP16) {
     sc0 = rep_half(ksc + (SLAB ? 0 : si.k0()));
@@ -188,7 +190,7 @@ __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, c
       uint32_t x0 = r0[0], x1 = r1[0];
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
-        mma_16816(acc[hb], hmul2(int4_lo_to_f16x2(x0), sc0), hmul2(int4_lo_to_f16x2(x1), sc1),
+        mma_16816(acc, hmul2(int4_lo_to_f16x2(x0), sc0), hmul2(int4_lo_to_f16x2(x1), sc1),
                   hmul2(int4_hi_to_f16x2(x0), sc0), hmul2(int4_hi_to_f16x2(x1), sc1),
                   qf[2 * j + hb][0], qf[2 * j + hb][1]);
         x0 >>= 8, x1 >>= 8;
@@ -197,7 +199,7 @@ __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, c
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
         const uint32_t lo = sel8(2 * hb), hi = sel8(2 * hb + 1);
-        mma_16816(acc[hb], hmul2(int8_to_f16x2(prmt(r0[0], r0[1], lo)), sc0),
+        mma_16816(acc, hmul2(int8_to_f16x2(prmt(r0[0], r0[1], lo)), sc0),
                   hmul2(int8_to_f16x2(prmt(r1[0], r1[1], lo)), sc1),
                   hmul2(int8_to_f16x2(prmt(r0[0], r0[1], hi)), sc0),
                   hmul2(int8_to_f16x2(prmt(r1[0], r1[1], hi)), sc1),
@@ -207,13 +209,13 @@ __device__ __forceinline__ void page_qk(const uint8_t *rec, const __half *ksc, c
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
         const uint32_t a0 = r0[hb], b0 = r0[2 + hb], a1 = r1[hb], b1 = r1[2 + hb];
-        mma_16816(acc[hb], prmt(a0, b0, 0x5410), prmt(a1, b1, 0x5410), prmt(a0, b0, 0x7632),
+        mma_16816(acc, prmt(a0, b0, 0x5410), prmt(a1, b1, 0x5410), prmt(a0, b0, 0x7632),
                   prmt(a1, b1, 0x7632), qf[2 * j + hb][0], qf[2 * j + hb][1]);
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) s[i] = acc[0][i] + acc[1][i];
+  for (int i = 0; i < 4; ++i) s[i] = acc[i];
 }
 
 // ------------------------------------------------------------------- P . V
