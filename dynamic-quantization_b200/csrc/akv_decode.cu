@@ -85,6 +85,24 @@ constexpr int64_t kHeaderBytes = 256;
 // Workspace: the header, then the partial states (kPartialsF holds their
 // offset in 4-byte words).
 
+// Division by a per-launch constant d for dividends 0 <= n < 2^31:
+// q = (umulhi(n, mul) + n) >> shift with shift = ceil(log2 d) and
+// mul = floor(2^32 (2^shift - d) / d) + 1 (Granlund and Montgomery, "Division
+// by invariant integers using multiplication", 1994).  Three instructions in
+// place of a runtime integer division.
+struct FastDiv {
+  uint32_t mul, shift;
+};
+__device__ __forceinline__ int fdiv(int n, FastDiv f) {
+  return (int)((__umulhi((uint32_t)n, f.mul) + (uint32_t)n) >> f.shift);
+}
+static FastDiv fast_div(uint32_t d) {  // d >= 1
+  uint32_t shift = 0;
+  while ((1ull << shift) < d) ++shift;
+  const uint64_t mul = ((1ull << 32) * ((1ull << shift) - d)) / d + 1;
+  return FastDiv{(uint32_t)mul, shift};
+}
+
 struct DecodeParams {
   const uint8_t *arena;
   int64_t arena_bytes;
@@ -96,6 +114,7 @@ struct DecodeParams {
   int64_t q_bs, q_hs;
   int32_t batch, q_heads, kv_heads, gqa, qgroups, items, log2_group;
   int32_t warps, range, smax, slot_heads;
+  FastDiv fd_mb, fd_ipb, fd_qgroups;  // max_blocks, kv_heads * qgroups, qgroups
   float scale_log2;
   int32_t *header;
   float *partials;
@@ -551,7 +570,7 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kMaxThreads, 1)
     raw = 0;
     nb = 0;
     if (e < e_end) {
-      const int it = e / mb, bb = it / ipb;
+      const int it = fdiv(e, p.fd_mb), bb = fdiv(it, p.fd_ipb);
       nb = p.seq_blocks ? min(__ldg(p.seq_blocks + bb), mb) : mb;
       raw = __ldg(p.table + (int64_t)bb * p.table_stride + (e - it * mb));
     }
@@ -568,7 +587,7 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kMaxThreads, 1)
     int mode = AKV_MODE_SKIP;
     uint32_t rb = 0;
     if (e < e_end) {
-      const int it = e / mb, j = e - it * mb;
+      const int it = fdiv(e, p.fd_mb), j = e - it * mb;
       first = j == 0;
       mode = j < nb ? desc_mode(raw) : AKV_MODE_SKIP;
       rb = mode == AKV_MODE_FP16 ? rb16 : (mode == AKV_MODE_INT8 ? rb8 : rb4);
@@ -578,7 +597,7 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kMaxThreads, 1)
         set_status(p.status, AKV_DEV_BAD_DESCRIPTOR);
         ok = false;
       }
-      w_src = poff + (int64_t)((it % ipb) / p.qgroups) * rb;
+      w_src = poff + (int64_t)fdiv(it - fdiv(it, p.fd_ipb) * ipb, p.fd_qgroups) * rb;
       w_meta = (uint32_t)mode | ((uint32_t)desc_ntok(raw) << 4) | ((uint32_t)(it - first_item) << 16);
     }
     // An INT8 or INT4 page pairs with the next page of its item and mode in
@@ -697,22 +716,19 @@ __global__ void __launch_bounds__(DecodeTraits<D>::kMaxThreads, 1)
         start_p = 0;
       }
       if (start + need - tail > (uint32_t)T::kRing) break;  // wait for room
-      const int64_t src = __shfl_sync(0xffffffffu, w_src, k);
-      const int64_t src2 = __shfl_sync(0xffffffffu, w_src2, k);
-      const uint32_t meta = __shfl_sync(0xffffffffu, w_meta, k);
       const uint32_t slot = issued % T::kSlots;
-      if (lane == 0) {
+      if (lane == k) {  // the slot's leading lane holds its record(s) and issues the copies
         slot_start[slot] = start;
         slot_phys[slot] = start_p;
-        slot_meta[slot] = meta;
+        slot_meta[slot] = w_meta;
         // No proxy fence before the copy: every generic read of this ring
         // space has returned its value (consumed by the page math) already.
         const uint32_t bar = smem_u32(&bars[slot]);
         mbar_expect_tx(bar, need);
-        const bool pair = (meta & 4u) != 0;
+        const bool pair = (w_meta & 4u) != 0;
         const uint32_t rb = pair ? need >> 1 : need;
-        bulk_g2s(smem_u32(ring + start_p), p.arena + src, rb, bar);
-        if (pair) bulk_g2s(smem_u32(ring + start_p + rb), p.arena + src2, rb, bar);
+        bulk_g2s(smem_u32(ring + start_p), p.arena + w_src, rb, bar);
+        if (pair) bulk_g2s(smem_u32(ring + start_p + rb), p.arena + w_src2, rb, bar);
       }
       head = start + need;
       head_p = start_p + need;
@@ -1290,6 +1306,9 @@ static int decode_launch(const void *arena, int64_t arena_bytes, const int64_t *
   p.range = pl.range;
   p.smax = pl.smax;
   p.slot_heads = pl.slot_heads;
+  p.fd_mb = fast_div((uint32_t)std::max(max_blocks, 1));  // no page is divided when max_blocks is 0
+  p.fd_ipb = fast_div((uint32_t)(kv_heads * pl.qgroups));
+  p.fd_qgroups = fast_div((uint32_t)pl.qgroups);
   p.scale_log2 = scale * 1.4426950408889634f;  // scores in base 2: exp(x) = 2^(x log2 e)
   p.header = (int32_t *)workspace;
   p.partials = (float *)((uint8_t *)workspace + kHeaderBytes);
