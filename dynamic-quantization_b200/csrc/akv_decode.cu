@@ -985,137 +985,180 @@ __global__ void __launch_bounds__(1024) merge_wide_kernel(const int32_t *__restr
 
 // ======================================== cross-GPU merge over peer memory
 // One long sequence split over `world` GPUs: every rank decodes its page range
-// into partial states, then this kernel, per (sequence, query head) row,
-// (1) merges the rank's partials into one state (as merge_wide_kernel),
-// (2) stores that state into every rank's exchange buffer over NVLink (plain
-//     peer stores) and raises the row's flag there with a system-scope release,
-// (3) waits (bounded) until every rank's flag for the row carries this call's
-//     epoch, and (4) merges the world's states into the output.
-// A row's wait depends only on the same row's CTA on the other GPUs, which
-// stores before it waits, so no CTA waits on one that cannot run.
+// into partial states, then this kernel, per (sequence, query head) row:
+// (1) folds the rank's partials into `splits` part-states, one per CTA of the
+//     row (CTA s folds contributors s*32 + w, stride 32 * splits),
+// (2) stores each part-state into every rank's exchange buffer over NVLink
+//     (plain 8-byte peer stores, each carrying its own epoch tag),
+// (3) in the row's first CTA only, waits (bounded) until every part-state of
+//     every rank carries this call's epoch, and (4) merges them into the output.
+// The row's other CTAs store and exit, so no CTA waits on one that cannot run:
+// a waiting CTA's siblings come right after it in launch order, and the host
+// uses splits > 1 only while the whole grid fits the GPU at once.
 //
-// Exchange buffer of one rank (akv_exchange_bytes): fp32 states
-// [2][world][rows][D+2] (slot [e & 1][r] holds rank r's state of every row for
-// the calls of epoch parity e & 1), then uint32 flags [2][world][rows] (flag
-// [e & 1][r][row] = the epoch of the last call of that parity whose rank-r
-// state of the row has landed).  Buffers start zeroed; epochs start at 1.
+// Exchange words.  Every value travels as one 64-bit word: the fp32 bits in the
+// low half, the call's epoch in the high half.  A 64-bit store is single-copy
+// atomic, so a reader that sees the epoch in a word holds that word's value of
+// this call: no fence between the values and a flag, and no second trip over
+// NVLink for the flag (the low-latency protocol of NCCL's LL fifo lines, at
+// 64-bit granularity).  Buffer of one rank (akv_exchange_bytes): words
+// [2][world][splits][rows][D + 2], slot [e & 1][r][s] holding rank r's part s
+// of every row for the calls of epoch parity e & 1.  Buffers start zeroed;
+// epochs start at 1, so no stale word matches.
 //
 // Two parities make consecutive calls safe without any extra handshake: rank
 // A's call e + 2 writes the parity-(e & 1) slots again only after its call
-// e + 1 finished, which needed every peer's call-(e + 1) state of every row,
+// e + 1 finished, which needed every peer's call-(e + 1) parts of every row,
 // and a peer publishes e + 1 only after its whole call-e grid (every read of
 // the parity-(e & 1) slots) has completed: its decode of e + 1 waits for that
-// grid, and its exchange of e + 1 waits for the decode.  With one slot a fast
-// rank's call e + 1 could overwrite a state (and move the flag past e) that a
-// slower rank was still waiting for or reading.
+// grid, and its exchange of e + 1 waits for the decode.
 constexpr int kMaxPeers = 8;
 struct PeerBuffers {
   void *buf[kMaxPeers];
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_tagged(uint64_t *p, float a, float b, uint32_t epoch) {
+  const uint64_t hi = (uint64_t)epoch << 32;
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(hi | __float_as_uint(a)),
+               "l"(hi | __float_as_uint(b))
+               : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// Load two tagged words; true when both carry `epoch`.
+__device__ __forceinline__ bool ld_tagged(const uint64_t *p, uint32_t epoch, float &a, float &b) {
+  uint64_t x, y;
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(p) : "memory");
+  a = __uint_as_float((uint32_t)x), b = __uint_as_float((uint32_t)y);
+  return (uint32_t)(x >> 32) == epoch && (uint32_t)(y >> 32) == epoch;
 }
+// The 32 entries (one per warp) that a CTA folds in shared memory.  Rows are
+// padded to D + 1 floats, so the column a warp reduces spans all 32 banks.
+template <int D>
+struct FoldSmem {
+  float acc[32][D + 1];
+  float m[32], l[32];
+  int bad;
+};
+
+// Fold the 32 entries of `sm` into one state: lane k of every warp weighs
+// entry k, every warp reduces the max and the sum, and warp w reduces the VEC
+// dims [VEC * w, VEC * w + VEC) (the dims lane w owns in a row): five shuffle
+// steps per dim, instead of one warp walking the entries.  Every lane returns
+// the row's max `top`, sum `den` and warp w's VEC accumulator sums `num`.
+// An entry with max -inf (an empty share) weighs 0 (triton_decode.py:78).
+template <int D>
+__device__ __forceinline__ void cta_fold(const FoldSmem<D> &sm, int warp, int lane, float &top, float &den,
+                                         float (&num)[D / 32]) {
+  constexpr int VEC = D / 32;
+  const float mk = sm.m[lane];
+  top = mk;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, o));
+  const float e = mk == -INFINITY ? 0.f : ex2(mk - top);
+  den = e * sm.l[lane];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) num[i] = e * sm.acc[lane][VEC * warp + i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    den += __shfl_xor_sync(0xffffffffu, den, o);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) num[i] += __shfl_xor_sync(0xffffffffu, num[i], o);
+  }
+}
+
+// Exchange part-states per row: 4 CTAs per row while the grid stays within
+// 128 CTAs (every B200 holds that many 1024-thread CTAs at once), else 1.
+// world * splits <= 32 (at most 8 ranks): one waiting warp per part-state.
+__host__ __device__ constexpr int exchange_splits(int64_t rows) { return rows <= 32 ? 4 : rows <= 64 ? 2 : 1; }
 
 template <int D>
 __global__ void __launch_bounds__(1024) merge_exchange_kernel(const int32_t *__restrict__ header, int q_heads,
-                                                              PeerBuffers peers, int rank, int world,
+                                                              int splits, const __grid_constant__ PeerBuffers peers,
+                                                              int rank, int world,
                                                               uint32_t epoch, __half *__restrict__ out,
                                                               int64_t obs, int64_t ohs, int32_t *status) {
-  constexpr int PS = D + 4, VEC = D / 32, W = 32, RS = D + 2;
-  __shared__ float sm_acc[W][D];
-  __shared__ float sm_m[W], sm_l[W];
+  constexpr int VEC = D / 32, W = 32, RW = D + 2;
+  static_assert(VEC % 2 == 0, "values travel two words per store");
+  __shared__ FoldSmem<D> sm;
   grid_dependency_wait();
+  // The next kernel may be placed on SMs this grid leaves free once every CTA
+  // of it has started; it still waits for this grid to complete.
+  allow_dependents_launch();
   MergeGeom g;
   if (!merge_geom<D>(header, g)) {
     if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
     return;
   }
-  const int h = blockIdx.x, b = blockIdx.y;
+  const int h = blockIdx.x / splits, s = blockIdx.x - h * splits, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = h / g.gqa, r = h - kvh * g.gqa, qg = r >> 3, n = r & 7;
   const int item = (b * g.kv_heads + kvh) * g.qgroups + qg;
+  if (threadIdx.x == 0) sm.bad = 0;
   float m = -INFINITY, l = 0.f, acc[VEC];
 #pragma unroll
   for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
-  if (g.mb > 0) {  // (1) this rank's partials, warp w folding contributors w, w + 32, ...
+  if (g.mb > 0) {  // (1) this CTA's share of the rank's partials
     const int w0 = item * g.mb / g.range;
-    fold_partials<D>(g, item, n, w0 + warp, min(((item + 1) * g.mb - 1) / g.range, g.warps - 1), W, lane, m, l,
-                     acc);
+    fold_partials<D>(g, item, n, w0 + s * W + warp, min(((item + 1) * g.mb - 1) / g.range, g.warps - 1),
+                     W * splits, lane, m, l, acc);
   }
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) sm_acc[warp][VEC * lane + i] = acc[i];
-  if (lane == 0) sm_m[warp] = m, sm_l[warp] = l;
+  for (int i = 0; i < VEC; ++i) sm.acc[warp][VEC * lane + i] = acc[i];
+  if (lane == 0) sm.m[warp] = m, sm.l[warp] = l;
   __syncthreads();
-  if (warp != 0) return;
-  float top = -INFINITY;
-#pragma unroll
-  for (int k = 0; k < W; ++k) top = fmaxf(top, sm_m[k]);
-  float num[VEC], den = 0.f;
-#pragma unroll
-  for (int i = 0; i < VEC; ++i) num[i] = 0.f;
-#pragma unroll 8
-  for (int k = 0; k < W; ++k) {
-    const float e = sm_m[k] == -INFINITY ? 0.f : ex2(sm_m[k] - top);
-    den += e * sm_l[k];
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) num[i] += e * sm_acc[k][VEC * lane + i];
-  }
-  const int rows = gridDim.x * gridDim.y, row = b * q_heads + h;
+  float top, den, num[VEC];
+  cta_fold<D>(sm, warp, lane, top, den, num);
+  const int64_t rows = (int64_t)q_heads * gridDim.y, row = (int64_t)b * q_heads + h;
   const int64_t par = epoch & 1u;
-  const int64_t flag_offset = 2ll * world * rows * RS;  // in floats: the flags follow both parities' states
-  // (2) publish to every rank, this one included, into this epoch parity's slots
-  for (int pr = 0; pr < world; ++pr) {
-    float *st = reinterpret_cast<float *>(peers.buf[pr]) + ((par * world + rank) * rows + row) * RS;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) st[VEC * lane + i] = num[i];
-    if (lane == 0) st[D] = top, st[D + 1] = den;
-  }
-  __threadfence_system();  // each lane's state stores before any flag
-  __syncwarp();
-  if (lane < world)
-    st_release_sys(reinterpret_cast<uint32_t *>(reinterpret_cast<float *>(peers.buf[lane]) + flag_offset) +
-                       (par * world + rank) * rows + row,
-                   epoch);
-  // (3) bounded wait for every rank's state of this row (lane q watches rank q)
-  const float *mine = reinterpret_cast<const float *>(peers.buf[rank]) + par * world * rows * RS;
-  const uint32_t *flags =
-      reinterpret_cast<const uint32_t *>(reinterpret_cast<const float *>(peers.buf[rank]) + flag_offset) +
-      par * world * rows;
-  bool ok = true;
+  // (2) lane p of warp w stores dims [VEC w, VEC w + VEC) of this part, and
+  // warp 0 its max and sum, into rank p's slot [parity][rank][s][row]
   if (lane < world) {
+    uint64_t *dst = reinterpret_cast<uint64_t *>(peers.buf[lane]) +
+                    (((par * world + rank) * splits + s) * rows + row) * RW;
+#pragma unroll
+    for (int i = 0; i < VEC; i += 2) st_tagged(dst + VEC * warp + i, num[i], num[i + 1], epoch);
+    if (warp == 0) st_tagged(dst + D, top, den, epoch);
+  }
+  if (s != 0) return;  // the row's first CTA merges
+  __syncthreads();     // every warp has read sm
+  // (3) warp q waits (bounded) for part q % splits of rank q / splits
+  const int parts = world * splits;
+  float mq = -INFINITY, lq = 0.f, aq[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) aq[i] = 0.f;
+  if (warp < parts) {
+    const int src = warp / splits, sp = warp - src * splits;
+    const uint64_t *st = reinterpret_cast<const uint64_t *>(peers.buf[rank]) +
+                         (((par * world + src) * splits + sp) * rows + row) * RW;
     const uint64_t t0 = globaltimer();
-    while (ld_acquire_sys(flags + (int64_t)lane * rows + row) != epoch)
+    while (true) {
+      bool got = ld_tagged(st + D, epoch, mq, lq);
+#pragma unroll
+      for (int i = 0; i < VEC; i += 2) got &= ld_tagged(st + VEC * lane + i, epoch, aq[i], aq[i + 1]);
+      if (got) break;
       if (globaltimer() - t0 > kWaitNs) {
-        ok = false;
+        sm.bad = 1;
+        mq = -INFINITY;
         break;
       }
+    }
   }
-  if (!__all_sync(0xffffffffu, ok)) {
-    if (lane == 0) set_status(status, AKV_DEV_TIMEOUT);
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) sm.acc[warp][VEC * lane + i] = aq[i];
+  if (lane == 0) sm.m[warp] = mq, sm.l[warp] = lq;
+  __syncthreads();
+  if (sm.bad) {
+    if (threadIdx.x == 0) set_status(status, AKV_DEV_TIMEOUT);
     return;
   }
-  // (4) merge the world's states (each lane re-acquires the flag it reads behind)
-  float mt = -INFINITY, lt = 0.f, at[VEC];
+  // (4) merge the world's parts; warp w writes output dims [VEC w, VEC w + VEC)
+  cta_fold<D>(sm, warp, lane, top, den, num);
+  if (lane < VEC) {
+    float v = num[0];
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) at[i] = 0.f;
-  for (int q = 0; q < world; ++q) {
-    (void)ld_acquire_sys(flags + (int64_t)q * rows + row);
-    const float *st = mine + ((int64_t)q * rows + row) * RS;
-    const float mq = __ldcg(st + D), lq = __ldcg(st + D + 1);
-    if (mq == -INFINITY) continue;
-    const float tp = fmaxf(mt, mq), c = ex2(mt - tp), e = ex2(mq - tp);
-    lt = lt * c + e * lq;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) at[i] = at[i] * c + e * __ldcg(st + VEC * lane + i);
-    mt = tp;
+    for (int i = 1; i < VEC; ++i)
+      if (lane == i) v = num[i];
+    out[(int64_t)b * obs + (int64_t)h * ohs + VEC * warp + lane] = __float2half_rn(v * (den > 0.f ? 1.f / den : 0.f));
   }
-  store_row<D>(lane, b, h, q_heads, mt, lt, at, out, obs, ohs, nullptr);
 }
 
 // Merge n already-merged states laid out [n][batch][q_heads][D+2] (e.g. gathered
@@ -1372,7 +1415,7 @@ extern "C" int64_t akv_exchange_bytes(int32_t world, int32_t batch, int32_t q_he
   if (world <= 0 || world > kMaxPeers || batch <= 0 || q_heads <= 0 || (head_dim != 64 && head_dim != 128))
     return -1;
   const int64_t rows = (int64_t)batch * q_heads;
-  return 2 * (world * rows * (head_dim + 2) * 4 + world * rows * 4);  // both epoch parities
+  return 2 * world * exchange_splits(rows) * rows * (head_dim + 2) * 8;  // both epoch parities, 8-byte words
 }
 
 extern "C" int akv_merge_exchange(const void *workspace, int32_t batch, int32_t q_heads, int32_t head_dim,
@@ -1389,13 +1432,14 @@ extern "C" int akv_merge_exchange(const void *workspace, int32_t batch, int32_t 
   }
   const int32_t *header = (const int32_t *)workspace;
   cudaStream_t s = (cudaStream_t)stream;
-  const dim3 grid(q_heads, batch);
+  const int splits = exchange_splits((int64_t)batch * q_heads);
+  const dim3 grid(q_heads * splits, batch);
   const cudaError_t err =
-      head_dim == 64 ? launch_dependent(merge_exchange_kernel<64>, grid, 1024, 0, s, header, (int)q_heads, peers,
-                                        (int)rank, (int)world, epoch, (__half *)out, out_batch_stride,
+      head_dim == 64 ? launch_dependent(merge_exchange_kernel<64>, grid, 1024, 0, s, header, (int)q_heads, splits,
+                                        peers, (int)rank, (int)world, epoch, (__half *)out, out_batch_stride,
                                         out_head_stride, dev_status)
-                     : launch_dependent(merge_exchange_kernel<128>, grid, 1024, 0, s, header, (int)q_heads, peers,
-                                        (int)rank, (int)world, epoch, (__half *)out, out_batch_stride,
+                     : launch_dependent(merge_exchange_kernel<128>, grid, 1024, 0, s, header, (int)q_heads, splits,
+                                        peers, (int)rank, (int)world, epoch, (__half *)out, out_batch_stride,
                                         out_head_stride, dev_status);
   return err == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
 }

@@ -207,16 +207,19 @@ int akv_merge_states(const float *states, int32_t n, int32_t batch, int32_t q_he
                      int64_t out_head_stride, void *stream);
 
 /* Bytes of one rank's exchange buffer for akv_merge_exchange (-1 if invalid):
- * fp32 states [2][world][batch * q_heads][head_dim + 2] then uint32 flags
- * [2][world][batch * q_heads], the leading 2 being the epoch parity.  world <= 8. */
+ * 64-bit words [2][world][splits][batch * q_heads][head_dim + 2], the leading
+ * 2 being the epoch parity, each word an fp32 value in its low half and the
+ * epoch of the call that wrote it in its high half; splits (part-states per
+ * row) is 4 for up to 32 rows, 2 for up to 64, else 1.  world <= 8. */
 int64_t akv_exchange_bytes(int32_t world, int32_t batch, int32_t q_heads, int32_t head_dim);
 
 /* Cross-GPU merge over peer memory for one sequence split over `world` GPUs
  * (each rank decoded its page range into `workspace` with akv_decode_partials):
- * one kernel merges this rank's partials per (sequence, query head), stores the
- * state into every rank's exchange buffer (plain peer stores over NVLink),
- * raises the row's flag there, waits (bounded, AKV_DEV_TIMEOUT after 2 s) for
- * every rank's flag of the row, and merges the world's states into `out`.
+ * one kernel merges this rank's partials per (sequence, query head) into
+ * part-states, stores them into every rank's exchange buffer (plain peer
+ * stores over NVLink, every 8-byte word tagged with the epoch), waits
+ * (bounded, AKV_DEV_TIMEOUT after 2 s) until every rank's parts of the row
+ * carry the epoch, and merges them into `out`.
  * Replaces akv_merge + an all-gather + akv_merge_states.
  *   peer_buffers[r]: rank r's exchange buffer as mapped in this process
  *     (akv_ipc_alloc / akv_ipc_open), zeroed before the first call;
