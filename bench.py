@@ -886,7 +886,7 @@ def long_context_leg(args, device, rank: int, world: int, local: int, wl: dict =
         "pct_of_hbm_peak": round(100 * step_bytes / (ms * 1e-3) / 1e9 / world / peak, 2),
         "decode_ms_max_over_ranks": round(dec_max, 5),
         "decode_ms_rank0": round(dec_ms, 5),
-        "combine_kernel": "merge_exchange_kernel (NVLink peer stores, bounded flag waits)" if world > 1
+        "combine_kernel": "merge_exchange_kernel (epoch-tagged NVLink peer stores, bounded waits)" if world > 1
         else "merge_wide_kernel (local partials into the output)",
         "combine_ms_max_over_ranks": round(comb_max, 5),
         "nccl_variant_ms_per_step": round(nccl_max, 5),

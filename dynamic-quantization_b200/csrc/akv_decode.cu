@@ -932,16 +932,50 @@ __device__ __forceinline__ void fold_partials(const MergeGeom &g, int item, int 
   }
 }
 
+// The 32 entries (one per warp) that a CTA folds in shared memory.  Rows are
+// padded to D + 1 floats, so the column a warp reduces spans all 32 banks.
+template <int D>
+struct FoldSmem {
+  float acc[32][D + 1];
+  float m[32], l[32];
+  int bad;
+};
+
+// Fold the 32 entries of `sm` into one state: lane k of every warp weighs
+// entry k, every warp reduces the max and the sum, and warp w reduces the VEC
+// dims [VEC * w, VEC * w + VEC) (the dims lane w owns in a row): five shuffle
+// steps per dim, instead of one warp walking the entries.  Every lane returns
+// the row's max `top`, sum `den` and warp w's VEC accumulator sums `num`.
+// An entry with max -inf (an empty share) weighs 0 (triton_decode.py:78).
+template <int D>
+__device__ __forceinline__ void cta_fold(const FoldSmem<D> &sm, int warp, int lane, float &top, float &den,
+                                         float (&num)[D / 32]) {
+  constexpr int VEC = D / 32;
+  const float mk = sm.m[lane];
+  top = mk;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, o));
+  const float e = mk == -INFINITY ? 0.f : ex2(mk - top);
+  den = e * sm.l[lane];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) num[i] = e * sm.acc[lane][VEC * warp + i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    den += __shfl_xor_sync(0xffffffffu, den, o);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) num[i] += __shfl_xor_sync(0xffffffffu, num[i], o);
+  }
+}
+
 // The same merge for rows with hundreds of contributors (a long single
 // sequence): one CTA of 32 warps per row, warp w folds contributors w, w+32, ...
-// and the warps combine in shared memory.
+// and the 32 warp states fold in shared memory (cta_fold).
 template <int D>
 __global__ void __launch_bounds__(1024) merge_wide_kernel(const int32_t *__restrict__ header, int q_heads,
                                                           __half *__restrict__ out, int64_t obs, int64_t ohs,
                                                           float *__restrict__ state, int32_t *status) {
-  constexpr int PS = D + 4, VEC = D / 32, W = 32;
-  __shared__ float sm_acc[W][D];
-  __shared__ float sm_m[W], sm_l[W];
+  constexpr int VEC = D / 32, W = 32;
+  __shared__ FoldSmem<D> sm;
   grid_dependency_wait();
   allow_dependents_launch();
   MergeGeom g;
@@ -962,24 +996,24 @@ __global__ void __launch_bounds__(1024) merge_wide_kernel(const int32_t *__restr
                      acc);
   }
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) sm_acc[warp][VEC * lane + i] = acc[i];
-  if (lane == 0) sm_m[warp] = m, sm_l[warp] = l;
+  for (int i = 0; i < VEC; ++i) sm.acc[warp][VEC * lane + i] = acc[i];
+  if (lane == 0) sm.m[warp] = m, sm.l[warp] = l;
   __syncthreads();
-  if (warp == 0) {
-    float top = -INFINITY;
+  float top, den, num[VEC];
+  cta_fold<D>(sm, warp, lane, top, den, num);
+  // warp w writes dims [VEC w, VEC w + VEC), lane i < VEC dim VEC w + i
+  if (lane < VEC) {
+    float v = num[0];
 #pragma unroll
-    for (int k = 0; k < W; ++k) top = fmaxf(top, sm_m[k]);
-    float num[VEC], den = 0.f;
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) num[i] = 0.f;
-#pragma unroll 8
-    for (int k = 0; k < W; ++k) {
-      const float e = sm_m[k] == -INFINITY ? 0.f : ex2(sm_m[k] - top);
-      den += e * sm_l[k];
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) num[i] += e * sm_acc[k][VEC * lane + i];
+    for (int i = 1; i < VEC; ++i)
+      if (lane == i) v = num[i];
+    if (out)
+      out[(int64_t)b * obs + (int64_t)h * ohs + VEC * warp + lane] = __float2half_rn(v * (den > 0.f ? 1.f / den : 0.f));
+    if (state) {
+      float *st = state + ((int64_t)b * q_heads + h) * (D + 2);
+      st[VEC * warp + lane] = v;
+      if (warp == 0 && lane == 0) st[D] = top, st[D + 1] = den;
     }
-    store_row<D>(lane, b, h, q_heads, top, den, num, out, obs, ohs, state);
   }
 }
 
@@ -1030,41 +1064,6 @@ __device__ __forceinline__ bool ld_tagged(const uint64_t *p, uint32_t epoch, flo
   a = __uint_as_float((uint32_t)x), b = __uint_as_float((uint32_t)y);
   return (uint32_t)(x >> 32) == epoch && (uint32_t)(y >> 32) == epoch;
 }
-// The 32 entries (one per warp) that a CTA folds in shared memory.  Rows are
-// padded to D + 1 floats, so the column a warp reduces spans all 32 banks.
-template <int D>
-struct FoldSmem {
-  float acc[32][D + 1];
-  float m[32], l[32];
-  int bad;
-};
-
-// Fold the 32 entries of `sm` into one state: lane k of every warp weighs
-// entry k, every warp reduces the max and the sum, and warp w reduces the VEC
-// dims [VEC * w, VEC * w + VEC) (the dims lane w owns in a row): five shuffle
-// steps per dim, instead of one warp walking the entries.  Every lane returns
-// the row's max `top`, sum `den` and warp w's VEC accumulator sums `num`.
-// An entry with max -inf (an empty share) weighs 0 (triton_decode.py:78).
-template <int D>
-__device__ __forceinline__ void cta_fold(const FoldSmem<D> &sm, int warp, int lane, float &top, float &den,
-                                         float (&num)[D / 32]) {
-  constexpr int VEC = D / 32;
-  const float mk = sm.m[lane];
-  top = mk;
-#pragma unroll
-  for (int o = 16; o; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, o));
-  const float e = mk == -INFINITY ? 0.f : ex2(mk - top);
-  den = e * sm.l[lane];
-#pragma unroll
-  for (int i = 0; i < VEC; ++i) num[i] = e * sm.acc[lane][VEC * warp + i];
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    den += __shfl_xor_sync(0xffffffffu, den, o);
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) num[i] += __shfl_xor_sync(0xffffffffu, num[i], o);
-  }
-}
-
 // Exchange part-states per row: 4 CTAs per row while the grid stays within
 // 128 CTAs (every B200 holds that many 1024-thread CTAs at once), else 1.
 // world * splits <= 32 (at most 8 ranks): one waiting warp per part-state.

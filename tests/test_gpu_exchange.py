@@ -100,6 +100,61 @@ def test_exchange_wait_runs_out_and_reports(cuda):
         _lib.call("akv_ipc_free", ctypes.c_void_p(ptr))
 
 
+def _tagged(values, epoch):
+    """Exchange words of fp32 values: the value's bits in the low half, the epoch in the high half."""
+    return (values.contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF) | (epoch << 32)
+
+
+@pytest.mark.parametrize("world, me", [(2, 0), (2, 1), (4, 2), (8, 5)])
+def test_exchange_merges_every_rank_on_one_gpu(cuda, world, me):
+    """The multi-rank merge on one GPU, with no kernel waiting on another
+    kernel: the other ranks' part-states are in this rank's exchange buffer
+    before the call, tagged with the call's epoch, as their kernels would have
+    stored them over NVLink (rank r's first part = its page range decoded to a
+    state by decode_partial_states, its other parts empty).  Rank `me` decodes
+    its own range and runs the exchange kernel; three epochs alternate the
+    parity halves.  The output matches the oracle over the whole sequence, and
+    this rank's own parts land in every rank's buffer tagged with the epoch."""
+    from anchorkv_b200.sharded import shard_range
+
+    k, v, q, bits = _sequence()
+    qd = q.to(cuda)
+    lib = _lib.load()
+    states = {}
+    for r in range(world):
+        if r != me:
+            lo, hi = shard_range(PAGES, r, world)
+            states[r] = akv.decode_partial_states(qd, _store(cuda, k, v, bits, lo, hi), 0.088)[0]  # [HQ, D + 2]
+    lo, hi = shard_range(PAGES, me, world)
+    store = _store(cuda, k, v, bits, lo, hi)
+    ws = torch.empty(lib.akv_workspace_bytes(1, HQ, HKV, D, store.max_blocks, 0), dtype=torch.uint8, device=cuda)
+    nbytes = lib.akv_exchange_bytes(world, 1, HQ, D)
+    splits = nbytes // (2 * world * HQ * (D + 2) * 8)
+    assert nbytes == 2 * world * splits * HQ * (D + 2) * 8 and splits in (1, 2, 4)
+    bufs = [torch.zeros(nbytes // 8, dtype=torch.int64, device=cuda) for _ in range(world)]
+    words = [b.view(2, world, splits, HQ, D + 2) for b in bufs]
+    peers = (ctypes.c_void_p * world)(*[b.data_ptr() for b in bufs])
+    empty = torch.zeros((HQ, D + 2), dtype=torch.float32, device=cuda)
+    empty[:, D] = -math.inf
+    oracle = _oracle()
+    for epoch in (1, 2, 3):
+        par = epoch & 1
+        for r, st in states.items():  # what rank r's kernel would have stored into this rank's buffer
+            words[me][par, r, 0] = _tagged(st, epoch)
+            for s in range(1, splits):
+                words[me][par, r, s] = _tagged(empty, epoch)
+        out = torch.full_like(qd, float("nan"))
+        _decode(store, qd, ws)
+        _lib.call("akv_merge_exchange", ws.data_ptr(), 1, HQ, D, peers, me, world, epoch, out.data_ptr(),
+                  out.stride(0), out.stride(1), _lib.status_word(cuda).data_ptr(),
+                  torch.cuda.current_stream(cuda).cuda_stream)
+        torch.cuda.synchronize(cuda)
+        assert akv.take_device_status(cuda) == 0
+        np.testing.assert_allclose(out.float().cpu().numpy().reshape(-1), oracle.reshape(-1), atol=2e-3, rtol=1e-2)
+        for r in range(world):  # this rank's parts, in every rank's buffer, carry the epoch
+            assert bool(((words[r][par, me] >> 32) == epoch).all())
+
+
 def _rank_main(rank, world, port, queue, epochs=3, delay_rank=None):
     """One rank: its shard of the sequence, ``epochs`` back-to-back calls of
     PeerExchange.attention and one of the NCCL all-gather form.  Rank
