@@ -2,9 +2,10 @@
 the long-context exchange of the reference's split-K merge
 (triton_decode.py:70-82) across GPUs, against the oracle.
 
-Single-GPU cases call the kernel with one rank, or make its bounded wait run
-out on a flag nothing sets; the two-rank case runs as two child processes, one
-GPU each (skipped with fewer GPUs), with NVLS off."""
+Single-GPU cases call the kernel with one rank, make its bounded wait run out
+on a rank that never stores, or give it the other ranks' parts in its buffer
+beforehand; the two-rank cases run as two child processes, one GPU each
+(skipped with fewer GPUs), with NVLS off."""
 
 import ctypes
 import math
@@ -34,6 +35,14 @@ def _sequence(seed=41):
     return k, v, q, bits
 
 
+def _sequence_batch(batch, seed=141):
+    k = W.outlier_kv(seed, (batch, HKV, 16 * PAGES, D))
+    v = W.outlier_kv(seed + 1, (batch, HKV, 16 * PAGES, D))
+    q = W.normal(seed + 2, (batch, HQ, 1, D))
+    bits = np.array([W.draw_modes(seed + 3 + b, PAGES, {16: .05, 8: .25, 4: .7}) for b in range(batch)])
+    return k, v, q, bits
+
+
 def _store(device, k, v, bits, lo, hi):
     sub = bits[:, lo:hi]
     pool = P.PagePool(HKV, D, group=2048, pages={b: int((sub == b).sum()) for b in (16, 8, 4)}, device=device)
@@ -47,12 +56,12 @@ def _buffer(world):
     return ptr.value
 
 
-def _decode(store, q, ws):
+def _decode(store, q, ws, batch=1):
     lib = _lib.load()
     stream = torch.cuda.current_stream(q.device).cuda_stream
     _lib.call("akv_decode_partials", store.pool.arena.data_ptr(), store.pool.nbytes, store.table.data_ptr(),
               store.table.stride(0), store.seq_blocks.data_ptr(), store.max_blocks, q.data_ptr(), q.stride(0),
-              q.stride(1), 1, HQ, HKV, D, 2048, 0.088, 0, ws.data_ptr(), ws.numel(),
+              q.stride(1), batch, HQ, HKV, D, 2048, 0.088, 0, ws.data_ptr(), ws.numel(),
               _lib.status_word(q.device).data_ptr(), stream)
 
 
@@ -76,9 +85,9 @@ def test_single_rank_exchange_equals_packed_attention(cuda):
 
 
 def test_exchange_wait_runs_out_and_reports(cuda):
-    """Rank 0 of a two-rank exchange whose other rank never publishes: the
-    flag nothing sets makes the bounded wait give up (2 s), the status word
-    reports AKV_DEV_TIMEOUT and the context stays usable."""
+    """Rank 0 of a two-rank exchange whose other rank never stores: the words
+    that never carry the epoch make the bounded wait give up (2 s), the status
+    word reports AKV_DEV_TIMEOUT and the context stays usable."""
     k, v, q, bits = _sequence()
     store = _store(cuda, k, v, bits, 0, PAGES // 2)
     qd = q.to(cuda)
@@ -105,8 +114,8 @@ def _tagged(values, epoch):
     return (values.contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF) | (epoch << 32)
 
 
-@pytest.mark.parametrize("world, me", [(2, 0), (2, 1), (4, 2), (8, 5)])
-def test_exchange_merges_every_rank_on_one_gpu(cuda, world, me):
+@pytest.mark.parametrize("world, me, batch", [(2, 0, 1), (2, 1, 1), (4, 2, 1), (8, 5, 1), (2, 1, 2), (4, 3, 4)])
+def test_exchange_merges_every_rank_on_one_gpu(cuda, world, me, batch):
     """The multi-rank merge on one GPU, with no kernel waiting on another
     kernel: the other ranks' part-states are in this rank's exchange buffer
     before the call, tagged with the call's epoch, as their kernels would have
@@ -114,29 +123,34 @@ def test_exchange_merges_every_rank_on_one_gpu(cuda, world, me):
     state by decode_partial_states, its other parts empty).  Rank `me` decodes
     its own range and runs the exchange kernel; three epochs alternate the
     parity halves.  The output matches the oracle over the whole sequence, and
-    this rank's own parts land in every rank's buffer tagged with the epoch."""
+    this rank's own parts land in every rank's buffer tagged with the epoch.
+    Batches of 1, 2 and 4 sequences give 32, 64 and 128 rows: four, two and one
+    part-states per row."""
     from anchorkv_b200.sharded import shard_range
 
-    k, v, q, bits = _sequence()
+    k, v, q, bits = _sequence() if batch == 1 else _sequence_batch(batch)
     qd = q.to(cuda)
     lib = _lib.load()
+    rows = batch * HQ
     states = {}
     for r in range(world):
         if r != me:
             lo, hi = shard_range(PAGES, r, world)
-            states[r] = akv.decode_partial_states(qd, _store(cuda, k, v, bits, lo, hi), 0.088)[0]  # [HQ, D + 2]
+            st = akv.decode_partial_states(qd, _store(cuda, k, v, bits, lo, hi), 0.088)  # [batch, HQ, D + 2]
+            states[r] = st.reshape(rows, D + 2)
     lo, hi = shard_range(PAGES, me, world)
     store = _store(cuda, k, v, bits, lo, hi)
-    ws = torch.empty(lib.akv_workspace_bytes(1, HQ, HKV, D, store.max_blocks, 0), dtype=torch.uint8, device=cuda)
-    nbytes = lib.akv_exchange_bytes(world, 1, HQ, D)
-    splits = nbytes // (2 * world * HQ * (D + 2) * 8)
-    assert nbytes == 2 * world * splits * HQ * (D + 2) * 8 and splits in (1, 2, 4)
+    ws = torch.empty(lib.akv_workspace_bytes(batch, HQ, HKV, D, store.max_blocks, 0), dtype=torch.uint8,
+                     device=cuda)
+    nbytes = lib.akv_exchange_bytes(world, batch, HQ, D)
+    splits = nbytes // (2 * world * rows * (D + 2) * 8)
+    assert nbytes == 2 * world * splits * rows * (D + 2) * 8 and splits == {32: 4, 64: 2, 128: 1}[rows]
     bufs = [torch.zeros(nbytes // 8, dtype=torch.int64, device=cuda) for _ in range(world)]
-    words = [b.view(2, world, splits, HQ, D + 2) for b in bufs]
+    words = [b.view(2, world, splits, rows, D + 2) for b in bufs]
     peers = (ctypes.c_void_p * world)(*[b.data_ptr() for b in bufs])
-    empty = torch.zeros((HQ, D + 2), dtype=torch.float32, device=cuda)
+    empty = torch.zeros((rows, D + 2), dtype=torch.float32, device=cuda)
     empty[:, D] = -math.inf
-    oracle = _oracle()
+    oracle = paged_decode_f64(q[:, :, 0].numpy(), k.numpy(), v.numpy(), bits, 0.088, group=2048)
     for epoch in (1, 2, 3):
         par = epoch & 1
         for r, st in states.items():  # what rank r's kernel would have stored into this rank's buffer
@@ -144,8 +158,8 @@ def test_exchange_merges_every_rank_on_one_gpu(cuda, world, me):
             for s in range(1, splits):
                 words[me][par, r, s] = _tagged(empty, epoch)
         out = torch.full_like(qd, float("nan"))
-        _decode(store, qd, ws)
-        _lib.call("akv_merge_exchange", ws.data_ptr(), 1, HQ, D, peers, me, world, epoch, out.data_ptr(),
+        _decode(store, qd, ws, batch)
+        _lib.call("akv_merge_exchange", ws.data_ptr(), batch, HQ, D, peers, me, world, epoch, out.data_ptr(),
                   out.stride(0), out.stride(1), _lib.status_word(cuda).data_ptr(),
                   torch.cuda.current_stream(cuda).cuda_stream)
         torch.cuda.synchronize(cuda)
