@@ -97,32 +97,61 @@ __device__ __forceinline__ int v_chunk_xor(int mode, int c, int lane) {
   return key << 4;
 }
 
-// Dequantize 8 consecutive elements of a record payload to fp16, exactly as
-// QuantizedPage.dense (packed_decode.py:34-45): fp16(int * float(scale)).
-// `vpay`: a V payload, stored in the swizzled byte order (v_swizzle).
-template <int D, int G, bool VPAY>
-__device__ __forceinline__ uint4 record_load8(int mode, const uint8_t *payload, const __half *sc,
-                                              int c, int lane) {
+// The payload bytes of 8 consecutive elements (e = 256 c + 8 lane) of a record:
+// FP16 all 16 bytes, INT8 8 bytes in .x / .y, INT4 4 bytes in .x.  `VPAY`: a V
+// payload, stored in the swizzled byte order (v_swizzle).
+template <int D, bool VPAY>
+__device__ __forceinline__ uint4 record_raw8(int mode, const uint8_t *payload, int c, int lane) {
   const int e = 256 * c + 8 * lane;
   const int vx = VPAY ? v_chunk_xor<D>(mode, c, lane) : 0;
   if (mode == AKV_MODE_FP16) return *reinterpret_cast<const uint4 *>(payload + ((2 * e) ^ vx));
-  const float s = __half2float(sc[e / G]);
-  int q[8];
   if (mode == AKV_MODE_INT8) {
     const uint2 w = *reinterpret_cast<const uint2 *>(payload + (e ^ vx));
+    return make_uint4(w.x, w.y, 0u, 0u);
+  }
+  return make_uint4(*reinterpret_cast<const uint32_t *>(payload + ((e / 2) ^ vx)), 0u, 0u, 0u);
+}
+
+// record_raw8 for all NC chunks of a slab, the mode tested once: the loads form
+// one straight-line batch.
+template <int D, int NC, bool VPAY>
+__device__ __forceinline__ void slab_raw(int mode, const uint8_t *payload, int lane, uint4 (&raw)[NC]) {
+  if (mode == AKV_MODE_FP16) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) raw[c] = record_raw8<D, VPAY>(AKV_MODE_FP16, payload, c, lane);
+  } else if (mode == AKV_MODE_INT8) {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) raw[c] = record_raw8<D, VPAY>(AKV_MODE_INT8, payload, c, lane);
+  } else {
+#pragma unroll
+    for (int c = 0; c < NC; ++c) raw[c] = record_raw8<D, VPAY>(AKV_MODE_INT4, payload, c, lane);
+  }
+}
+
+// The 8 integers of a raw INT8 / INT4 chunk.
+__device__ __forceinline__ void raw8_ints(int mode, uint4 w, int (&q)[8]) {
+  if (mode == AKV_MODE_INT8) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       q[i] = (int)(int8_t)(w.x >> (8 * i));
       q[4 + i] = (int)(int8_t)(w.y >> (8 * i));
     }
   } else {
-    const uint32_t w = *reinterpret_cast<const uint32_t *>(payload + ((e / 2) ^ vx));
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      int n = (w >> (4 * i)) & 15;
+      const int n = (w.x >> (4 * i)) & 15;
       q[i] = n >= 8 ? n - 16 : n;
     }
   }
+}
+
+// A raw chunk dequantized to fp16 exactly as QuantizedPage.dense
+// (packed_decode.py:34-45): fp16(int * float(scale)), `s` the element group's
+// scale (unused for FP16 pages).
+__device__ __forceinline__ uint4 raw8_to_f16(int mode, uint4 w, float s) {
+  if (mode == AKV_MODE_FP16) return w;
+  int q[8];
+  raw8_ints(mode, w, q);
   uint32_t h[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -133,16 +162,11 @@ __device__ __forceinline__ uint4 record_load8(int mode, const uint8_t *payload, 
   return make_uint4(h[0], h[1], h[2], h[3]);
 }
 
-// The same 8 elements as float values int * float(scale), before any rounding
-// to fp16 (PackedTensor.dequantize, backend.py:177-180, rounds once to the
-// caller's dtype).  FP16 pages give their stored values.
-template <int D, int G, bool VPAY>
-__device__ __forceinline__ void record_load8_f32(int mode, const uint8_t *payload, const __half *sc, int c,
-                                                 int lane, float (&x)[8]) {
-  const int e = 256 * c + 8 * lane;
-  const int vx = VPAY ? v_chunk_xor<D>(mode, c, lane) : 0;
+// A raw chunk as float values int * float(scale), before any rounding to fp16
+// (PackedTensor.dequantize, backend.py:177-180, rounds once to the caller's
+// dtype).  FP16 pages give their stored values.
+__device__ __forceinline__ void raw8_to_f32(int mode, uint4 w, float s, float (&x)[8]) {
   if (mode == AKV_MODE_FP16) {
-    const uint4 w = *reinterpret_cast<const uint4 *>(payload + ((2 * e) ^ vx));
     const uint32_t h[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -151,22 +175,24 @@ __device__ __forceinline__ void record_load8_f32(int mode, const uint8_t *payloa
     }
     return;
   }
-  const float s = __half2float(sc[e / G]);
-  if (mode == AKV_MODE_INT8) {
-    const uint2 w = *reinterpret_cast<const uint2 *>(payload + (e ^ vx));
+  int q[8];
+  raw8_ints(mode, w, q);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      x[i] = (float)(int)(int8_t)(w.x >> (8 * i)) * s;
-      x[4 + i] = (float)(int)(int8_t)(w.y >> (8 * i)) * s;
-    }
-  } else {
-    const uint32_t w = *reinterpret_cast<const uint32_t *>(payload + ((e / 2) ^ vx));
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int n = (w >> (4 * i)) & 15;
-      x[i] = (float)(n >= 8 ? n - 16 : n) * s;
-    }
-  }
+  for (int i = 0; i < 8; ++i) x[i] = (float)q[i] * s;
+}
+
+// The scale of chunk c's elements of lane `lane` (groups of G elements).
+template <int G>
+__device__ __forceinline__ float chunk_scale(int mode, const __half *sc, int c, int lane) {
+  return mode == AKV_MODE_FP16 ? 1.f : __half2float(sc[(256 * c + 8 * lane) / G]);
+}
+
+// Dequantize 8 consecutive elements of a record payload to fp16, exactly as
+// QuantizedPage.dense (packed_decode.py:34-45): fp16(int * float(scale)).
+template <int D, int G, bool VPAY>
+__device__ __forceinline__ uint4 record_load8(int mode, const uint8_t *payload, const __half *sc,
+                                              int c, int lane) {
+  return raw8_to_f16(mode, record_raw8<D, VPAY>(mode, payload, c, lane), chunk_scale<G>(mode, sc, c, lane));
 }
 
 // ---- exact quantization of a page slab without a division per element
@@ -530,28 +556,32 @@ __global__ void __launch_bounds__(256) unpack_pages_kernel(const int64_t *__rest
     const int64_t rb = record_bytes(D, G, mode);
     const bool ok = mode != AKV_MODE_SKIP && page_in_arena(d, rb * heads, arena_bytes);
     if (mode != AKV_MODE_SKIP && !ok && lane == 0) set_status(status, AKV_DEV_BAD_DESCRIPTOR);
+    // Every chunk's payload load is issued before any is converted or stored, so
+    // a warp keeps its whole slab in flight (one memory round trip per slab,
+    // not one per chunk).
+    uint4 raw[NC];
+    float s[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) raw[c] = make_uint4(0u, 0u, 0u, 0u), s[c] = 0.f;
+    if (ok) {
+      const uint8_t *rec = arena + desc_offset(d) + h * rb;
+      const int64_t pb = payload_bytes(D, mode);
+      const __half *sc = reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, mode);
+      if (kv)
+        slab_raw<D, NC, true>(mode, rec + pb, lane, raw);
+      else
+        slab_raw<D, NC, false>(mode, rec, lane, raw);
+#pragma unroll
+      for (int c = 0; c < NC; ++c) s[c] = chunk_scale<G>(mode, sc, c, lane);
+    }
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       OutT *dst = out + 256 * c + 8 * lane;
       if constexpr (sizeof(OutT) == 2 && !std::is_same<OutT, __nv_bfloat16>::value) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (ok) {
-          const uint8_t *rec = arena + desc_offset(d) + h * rb;
-          const int64_t pb = payload_bytes(D, mode);
-          const __half *sc = reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, mode);
-          v = kv ? record_load8<D, G, true>(mode, rec + pb, sc, c, lane)
-                 : record_load8<D, G, false>(mode, rec, sc, c, lane);
-        }
-        *reinterpret_cast<uint4 *>(dst) = v;
+        *reinterpret_cast<uint4 *>(dst) = ok ? raw8_to_f16(mode, raw[c], s[c]) : make_uint4(0u, 0u, 0u, 0u);
       } else {
         float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (ok) {
-          const uint8_t *rec = arena + desc_offset(d) + h * rb;
-          const int64_t pb = payload_bytes(D, mode);
-          const __half *sc = reinterpret_cast<const __half *>(rec + 2 * pb) + kv * scale_count(D, G, mode);
-          if (kv) record_load8_f32<D, G, true>(mode, rec + pb, sc, c, lane, x);
-          else record_load8_f32<D, G, false>(mode, rec, sc, c, lane, x);
-        }
+        if (ok) raw8_to_f32(mode, raw[c], s[c], x);
 #pragma unroll
         for (int i = 0; i < 8; ++i) dst[i] = from_f32<OutT>(x[i]);
       }
