@@ -1163,23 +1163,55 @@ __global__ void __launch_bounds__(1024) merge_exchange_kernel(const int32_t *__r
 // Merge n already-merged states laid out [n][batch][q_heads][D+2] (e.g. gathered
 // from n GPUs) into the normalised output.
 template <int D>
-__global__ void __launch_bounds__(D) merge_states_kernel(const float *__restrict__ states, int n,
-                                                         int q_heads, int batch, __half *__restrict__ out,
-                                                         int64_t obs, int64_t ohs) {
-  constexpr int RS = D + 2;
-  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+__global__ void __launch_bounds__(256) merge_states_kernel(const float *__restrict__ states, int n,
+                                                           int q_heads, int batch, __half *__restrict__ out,
+                                                           int64_t obs, int64_t ohs) {
+  // One warp per (sequence, query head) row, 8 rows per CTA; lane i owns dims
+  // [VEC i, VEC i + VEC).  The states' maxima are loaded lane-parallel, then
+  // the accumulators and sums 8 states at a time, every load of a batch issued
+  // before any is used; each lane sums in state order as one thread per dim
+  // would, so the result does not depend on the batching.
+  constexpr int RS = D + 2, VEC = D / 32, SB = 8;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= (int64_t)batch * q_heads) return;
+  const int b = (int)(row / q_heads), h = (int)(row - (int64_t)b * q_heads);
   const int64_t stride = (int64_t)batch * q_heads * RS;
-  const float *base = states + ((int64_t)b * q_heads + h) * RS;
+  const float *base = states + row * RS;
   float top = -INFINITY;
-  for (int s = 0; s < n; ++s) top = fmaxf(top, base[s * stride + D]);
-  float num = 0.f, den = 0.f;
-  for (int s = 0; s < n; ++s) {
-    const float m = base[s * stride + D];
-    const float wt = m == -INFINITY ? 0.f : ex2(m - top);
-    num += wt * base[s * stride + d];
-    den += wt * base[s * stride + D + 1];
+  for (int s0 = 0; s0 < n; s0 += 32)
+    if (s0 + lane < n) top = fmaxf(top, __ldg(base + (s0 + lane) * stride + D));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) top = fmaxf(top, __shfl_xor_sync(0xffffffffu, top, o));
+  float num[VEC], den = 0.f;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) num[i] = 0.f;
+  for (int s0 = 0; s0 < n; s0 += SB) {
+    float m[SB], l[SB], a[SB][VEC];
+#pragma unroll
+    for (int j = 0; j < SB; ++j) {
+      m[j] = -INFINITY, l[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) a[j][i] = 0.f;
+      if (s0 + j < n) {
+        const float *st = base + (s0 + j) * stride;
+        m[j] = __ldg(st + D), l[j] = __ldg(st + D + 1);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) a[j][i] = __ldg(st + VEC * lane + i);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < SB; ++j) {
+      if (s0 + j >= n) break;
+      const float wt = m[j] == -INFINITY ? 0.f : ex2(m[j] - top);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) num[i] += wt * a[j][i];
+      den += wt * l[j];
+    }
   }
-  out[(int64_t)b * obs + (int64_t)h * ohs + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+  __half *o = out + (int64_t)b * obs + (int64_t)h * ohs + VEC * lane;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) o[i] = __float2half_rn(den > 0.f ? num[i] / den : 0.f);
 }
 
 // ------------------------------------------------------------------- host
@@ -1476,13 +1508,14 @@ extern "C" int akv_merge_states(const float *states, int32_t n, int32_t batch, i
                                 int64_t out_head_stride, void *stream) {
   if (!states || !out || n <= 0 || batch <= 0 || q_heads <= 0 || batch > 65535) return AKV_ERR_INVALID;
   if (head_dim != 64 && head_dim != 128) return AKV_ERR_UNSUPPORTED;
-  const dim3 grid(q_heads, batch);
+  const int64_t rows = (int64_t)batch * q_heads;
+  const dim3 grid((unsigned)((rows + 7) / 8));
   cudaStream_t s = (cudaStream_t)stream;
   if (head_dim == 64)
-    merge_states_kernel<64><<<grid, 64, 0, s>>>(states, n, q_heads, batch, (__half *)out,
-                                                out_batch_stride, out_head_stride);
+    merge_states_kernel<64><<<grid, 256, 0, s>>>(states, n, q_heads, batch, (__half *)out,
+                                                 out_batch_stride, out_head_stride);
   else
-    merge_states_kernel<128><<<grid, 128, 0, s>>>(states, n, q_heads, batch, (__half *)out,
+    merge_states_kernel<128><<<grid, 256, 0, s>>>(states, n, q_heads, batch, (__half *)out,
                                                   out_batch_stride, out_head_stride);
   return cudaGetLastError() == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
 }
