@@ -18,7 +18,7 @@ extern "C" const char *akv_status_string(int status) {
 // 4: exchange buffers hold both epoch parities (akv_exchange_bytes doubled);
 //    akv_repack_pages takes the quantizer semantics, akv_unpack_pages the output dtype;
 //    status words may live in mapped pinned host memory (akv_status_alloc).
-extern "C" int akv_abi_version(void) { return 4; }
+extern "C" int akv_abi_version(void) { return 5; }
 
 // The status word in mapped pinned host memory: kernels write it through the
 // device address, the host reads it through the host address with no copy or

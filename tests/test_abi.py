@@ -28,7 +28,7 @@ def test_library_exports_declared_symbol(name):
 
 def test_host_helpers_need_no_gpu():
     lib = _lib.load()
-    assert lib.akv_abi_version() == 4
+    assert lib.akv_abi_version() == 5
     assert _lib.status_string(_lib.ERR_INVALID).startswith("invalid")
     for dim in (64, 128):
         for group in (32, 64, 128, 16 * dim):
