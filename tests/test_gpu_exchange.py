@@ -261,3 +261,54 @@ def test_two_rank_exchange_with_a_delayed_rank():
             np.testing.assert_array_equal(out, outs[0])  # the same inputs every epoch
         np.testing.assert_allclose(nccl.reshape(-1), outs[0].reshape(-1), atol=1e-3, rtol=1e-3)
     np.testing.assert_array_equal(results[0][1][-1], results[1][1][-1])
+
+
+def test_exchange_merges_every_rank_on_one_gpu_head_dim_64(cuda):
+    """The prefilled multi-rank merge at head_dim 64 (two words per lane, 66
+    words per state): 3 ranks, rank 2 here, 16 query / 4 KV heads."""
+    from anchorkv_b200.sharded import shard_range
+
+    hq, hkv, dim, pages, world, me = 16, 4, 64, 120, 3, 2
+    k = W.outlier_kv(61, (1, hkv, 16 * pages, dim))
+    v = W.outlier_kv(62, (1, hkv, 16 * pages, dim))
+    q = W.normal(63, (1, hq, 1, dim))
+    bits = np.array(W.draw_modes(64, pages, {16: .1, 8: .3, 4: .6}))[None]
+    qd = q.to(cuda)
+
+    def store(lo, hi):
+        sub = bits[:, lo:hi]
+        pool = P.PagePool(hkv, dim, group=16 * dim, pages={b: int((sub == b).sum()) for b in (16, 8, 4)},
+                          device=cuda)
+        return P.pack_dense(pool, k[:, :, 16 * lo:16 * hi].to(cuda), v[:, :, 16 * lo:16 * hi].to(cuda), sub)
+
+    lib = _lib.load()
+    states = {r: akv.decode_partial_states(qd, store(*shard_range(pages, r, world)), 0.1)[0]
+              for r in range(world) if r != me}
+    mine = store(*shard_range(pages, me, world))
+    ws = torch.empty(lib.akv_workspace_bytes(1, hq, hkv, dim, mine.max_blocks, 0), dtype=torch.uint8, device=cuda)
+    nbytes = lib.akv_exchange_bytes(world, 1, hq, dim)
+    splits = nbytes // (2 * world * hq * (dim + 2) * 8)
+    assert splits == 4
+    bufs = [torch.zeros(nbytes // 8, dtype=torch.int64, device=cuda) for _ in range(world)]
+    words = [b.view(2, world, splits, hq, dim + 2) for b in bufs]
+    peers = (ctypes.c_void_p * world)(*[b.data_ptr() for b in bufs])
+    empty = torch.zeros((hq, dim + 2), dtype=torch.float32, device=cuda)
+    empty[:, dim] = -math.inf
+    oracle = paged_decode_f64(q[:, :, 0].numpy(), k.numpy(), v.numpy(), bits, 0.1, group=16 * dim)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    for epoch in (1, 2, 3):
+        par = epoch & 1
+        for r, st in states.items():
+            words[me][par, r, 0] = _tagged(st, epoch)
+            for s in range(1, splits):
+                words[me][par, r, s] = _tagged(empty, epoch)
+        out = torch.full_like(qd, float("nan"))
+        _lib.call("akv_decode_partials", mine.pool.arena.data_ptr(), mine.pool.nbytes, mine.table.data_ptr(),
+                  mine.table.stride(0), mine.seq_blocks.data_ptr(), mine.max_blocks, qd.data_ptr(), qd.stride(0),
+                  qd.stride(1), 1, hq, hkv, dim, 16 * dim, 0.1, 0, ws.data_ptr(), ws.numel(),
+                  _lib.status_word(cuda).data_ptr(), stream)
+        _lib.call("akv_merge_exchange", ws.data_ptr(), 1, hq, dim, peers, me, world, epoch, out.data_ptr(),
+                  out.stride(0), out.stride(1), _lib.status_word(cuda).data_ptr(), stream)
+        torch.cuda.synchronize(cuda)
+        assert akv.take_device_status(cuda) == 0
+        np.testing.assert_allclose(out.float().cpu().numpy().reshape(-1), oracle.reshape(-1), atol=2e-3, rtol=1e-2)
