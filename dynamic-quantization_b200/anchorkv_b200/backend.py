@@ -49,11 +49,12 @@ from .policy import PRECISION_RANK, CacheMode, CachePlan, as_mode
 
 
 class BackendUnavailableError(RuntimeError):
-    """Raised when a required runtime dependency is unavailable."""
+    """A dependency of the data plane (torch, the CUDA library or a device) is missing."""
 
 
 class LossyPromotionError(RuntimeError):
-    """Raised when code attempts to restore precision that was already lost."""
+    """A segment was asked to move to a higher precision than it holds: its
+    quantized values cannot give back the bits they dropped."""
 
 
 class SegmentRole(str, Enum):
@@ -162,7 +163,9 @@ _KERNEL_DTYPES = {torch.float32: _lib.DTYPE_F32, torch.float16: _lib.DTYPE_F16,
 
 @dataclass(frozen=True, slots=True)
 class PackedTensor:
-    """A tensor stored as FP16, symmetric INT8, or packed symmetric INT4."""
+    """One tensor in a cache representation: fp16 values, or int8 / two-per-byte
+    int4 payload with one fp16 absmax scale per group of ``group_size``
+    elements (EVICTED keeps no payload)."""
 
     mode: CacheMode
     shape: tuple[int, ...]
