@@ -63,6 +63,31 @@ def _as_table(layer):
     return layer
 
 
+def _check_query(query, layer, splits, *, empty_ok: bool) -> int:
+    """The argument checks of triton_decode.py:86-94, in its order and with its
+    messages, for a page table of ``layer``; returns the batch.
+
+    ``empty_ok`` admits a table with no pages: a shard of a sequence split over
+    more ranks than it has pages decodes to an empty state (zero weight in the
+    LSE merge); an output needs at least one page, as in the reference."""
+    batched = isinstance(layer, PagedBatch)
+    batch = layer.batch if batched else 1
+    if query.dim() != 4 or query.shape[0] != batch or query.shape[2] != 1 or query.shape[-1] != layer.dim:
+        raise ValueError('packed kernel supports batch=1, query length=1 only' if not batched
+                         else 'query must be [batch, heads, 1, head_dim] for the page table')
+    length = layer.max_blocks if batched else layer.length
+    if query.dtype != torch.float16 or not query.is_cuda or (length == 0 and not empty_ok):
+        raise ValueError('packed kernel requires a nonempty CUDA FP16 cache')
+    if layer.dim not in (64, 128) or layer.block != 16 or not group_ok(layer.dim, layer.group):
+        raise ValueError('supported geometry: block=16, group=32/64/128 or one scale per '
+                         'block and head, head dim=64/128')
+    if query.shape[1] % layer.heads:
+        raise ValueError('query heads must be divisible by KV heads')
+    if splits < 0:
+        raise ValueError('splits must be non-negative')
+    return batch
+
+
 def packed_attention(query, layer, scale, splits=4, *, out=None):
     """Attend one query token per sequence over the layer's packed pages.
 
@@ -74,24 +99,14 @@ def packed_attention(query, layer, scale, splits=4, *, out=None):
     LSE (the reference's split-K knob); the decode cuts finer, down to 16 pages
     a piece, while the device has resident warps to spare (``0``: every
     resident warp).  Results do not depend on it beyond fp32 rounding.
+    ``out``: an optional fp16 CUDA tensor of the query's shape on its device.
     """
     layer = _as_table(layer)
-    batched = isinstance(layer, PagedBatch)
-    batch = layer.batch if batched else 1
-    if query.shape[0] != batch or query.shape[2] != 1 or query.shape[-1] != layer.dim:
-        raise ValueError('packed kernel supports batch=1, query length=1 only' if not batched
-                         else 'query must be [batch, heads, 1, head_dim] for the page table')
-    length = layer.max_blocks if batched else layer.length
-    if query.dtype != torch.float16 or not query.is_cuda or length == 0:
-        raise ValueError('packed kernel requires a nonempty CUDA FP16 cache')
-    if layer.dim not in (64, 128) or layer.block != 16 or not group_ok(layer.dim, layer.group):
-        raise ValueError('supported geometry: block=16, group=32/64/128 or one scale per '
-                         'block and head, head dim=64/128')
+    batch = _check_query(query, layer, splits, empty_ok=False)
     heads = query.shape[1]
-    if heads % layer.heads:
-        raise ValueError('query heads must be divisible by KV heads')
-    if splits < 0:
-        raise ValueError('splits must be non-negative')
+    if out is not None and (out.dtype != torch.float16 or tuple(out.shape) != tuple(query.shape)
+                            or out.device != query.device or out.stride(-1) != 1):
+        raise ValueError("out must be an FP16 tensor of the query's shape on its device, unit stride in head_dim")
     if query.stride(-1) != 1 or query.stride(1) % 8 or query.stride(0) % 8 or query.data_ptr() % 16:
         query = query.contiguous()
     arena, arena_bytes, table, seq_blocks, max_blocks = _store_geometry(layer)
@@ -116,10 +131,11 @@ def decode_partial_states(query, layer, scale, splits=0):
 
     Returns fp32 ``[batch, Hq, D + 2]`` = (acc[D], m, l) with ``m`` in base-2
     units of the scaled score, for a further merge (e.g. across GPUs holding
-    contiguous shards of each sequence) with :func:`merge_states`."""
+    contiguous shards of each sequence) with :func:`merge_states`.  The query
+    is checked as :func:`packed_attention` checks it, except that a table with
+    no pages is allowed (its state has zero weight in the merge)."""
     layer = _as_table(layer)
-    batched = isinstance(layer, PagedBatch)
-    batch = layer.batch if batched else 1
+    batch = _check_query(query, layer, splits, empty_ok=True)
     heads = query.shape[1]
     query = query.contiguous()
     arena, arena_bytes, table, seq_blocks, max_blocks = _store_geometry(layer)
@@ -143,6 +159,8 @@ def decode_partial_states(query, layer, scale, splits=0):
 def merge_states(states: torch.Tensor) -> torch.Tensor:
     """Merge ``[n, batch, Hq, D + 2]`` LSE states (e.g. gathered from n GPUs)
     into the normalised fp16 output ``[batch, Hq, 1, D]``."""
+    if states.dim() != 4 or states.dtype != torch.float32 or not states.is_cuda:
+        raise ValueError("states must be a CUDA float32 tensor [n, batch, heads, head_dim + 2]")
     n, batch, heads, rs = states.shape
     states = states.contiguous()
     out = torch.empty((batch, heads, 1, rs - 2), dtype=torch.float16, device=states.device)

@@ -29,7 +29,8 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .decode import _store_geometry, _workspace, decode_partial_states, merge_states
+from .decode import (_as_table, _check_query, _store_geometry, _workspace, decode_partial_states,
+                     merge_states)
 
 
 def shard_range(n_blocks: int, rank: int, world: int) -> tuple[int, int]:
@@ -107,9 +108,18 @@ class PeerExchange:
 
     def attention(self, query, local_store, scale, *, splits=0, out=None):
         """Decode this rank's pages of each sequence and merge with the other
-        ranks: the full-context output ``[batch, Hq, 1, D]`` on every rank."""
+        ranks: the full-context output ``[batch, Hq, 1, D]`` on every rank.
+
+        The query is checked as :func:`~anchorkv_b200.packed_attention` checks
+        it (a shard with no pages is allowed); ``out``, if given, is an fp16
+        tensor of the query's shape on its device."""
         if tuple(query.shape) != (self.batch, self.q_heads, 1, self.dim):
             raise ValueError("query shape differs from the exchange's geometry")
+        local_store = _as_table(local_store)
+        _check_query(query, local_store, splits, empty_ok=True)
+        if out is not None and (out.dtype != torch.float16 or tuple(out.shape) != tuple(query.shape)
+                                or out.device != query.device or out.stride(-1) != 1):
+            raise ValueError("out must be an FP16 tensor of the query's shape on its device, unit stride in head_dim")
         query = query.contiguous()
         arena, arena_bytes, table, seq_blocks, max_blocks = _store_geometry(local_store)
         dev = query.device

@@ -193,6 +193,50 @@ def test_cpu_tensors_are_refused_by_the_kernels():
         akv.pack_page(torch.randn(2, 16, 64), 4)
 
 
+class _Query:
+    """Shape, dtype and device of a query, without a tensor (the checks run before any launch)."""
+
+    def __init__(self, shape, dtype=torch.float16, is_cuda=True):
+        self.shape, self.dtype, self.is_cuda = torch.Size(shape), dtype, is_cuda
+
+    def dim(self):
+        return len(self.shape)
+
+
+def test_decode_arguments_are_checked_before_any_launch():
+    """decode_partial_states, merge_states and packed_attention refuse what the kernels would
+    misread (a query that is not CUDA fp16, states that are not float32), with the reference's
+    messages (triton_decode.py:86-94); only the partial-state decode admits a table with no pages."""
+    from anchorkv_b200.decode import _check_query
+
+    pool = P.PagePool(2, 64, group=1024, pages={16: 4, 8: 0, 4: 0}, device="cpu")
+    table, empty = P.PagedBatch(pool, 2, 3), P.PagedBatch(pool, 2, 0)
+    for bad in (torch.zeros(2, 4, 1, 64, dtype=torch.float16), torch.zeros(2, 4, 1, 64)):
+        with pytest.raises(ValueError, match="CUDA FP16"):
+            akv.decode_partial_states(bad, table, 0.1)
+        with pytest.raises(ValueError, match="CUDA FP16"):
+            akv.packed_attention(bad, table, 0.1)
+    with pytest.raises(ValueError, match="CUDA float32"):
+        akv.merge_states(torch.zeros(2, 2, 4, 66))  # a CPU tensor
+    with pytest.raises(ValueError, match="CUDA float32"):
+        akv.merge_states(torch.zeros(2, 4, 66))  # not [n, batch, heads, D + 2]
+
+    assert _check_query(_Query((2, 4, 1, 64)), table, 0, empty_ok=False) == 2
+    assert _check_query(_Query((2, 4, 1, 64)), empty, 0, empty_ok=True) == 2
+    with pytest.raises(ValueError, match="nonempty CUDA FP16 cache"):
+        _check_query(_Query((2, 4, 1, 64)), empty, 0, empty_ok=False)
+    with pytest.raises(ValueError, match="nonempty CUDA FP16 cache"):
+        _check_query(_Query((2, 4, 1, 64), dtype=torch.float32), empty, 0, empty_ok=True)
+    with pytest.raises(ValueError, match=r"\[batch, heads, 1, head_dim\]"):
+        _check_query(_Query((2, 4, 64)), table, 0, empty_ok=True)
+    with pytest.raises(ValueError, match=r"\[batch, heads, 1, head_dim\]"):
+        _check_query(_Query((1, 4, 1, 64)), table, 0, empty_ok=True)
+    with pytest.raises(ValueError, match="divisible by KV heads"):
+        _check_query(_Query((2, 3, 1, 64)), table, 0, empty_ok=True)
+    with pytest.raises(ValueError, match="non-negative"):
+        _check_query(_Query((2, 4, 1, 64)), table, -1, empty_ok=True)
+
+
 class _HostWord:
     """A status word in plain host memory standing in for the mapped pinned one."""
 
