@@ -316,9 +316,10 @@ __device__ __forceinline__ void store_slab(const uint4 (&v)[Slab<D>::kChunks], i
   }
   GroupScale gs{};
   float r = 0.f;
+  constexpr int kGroupChunks = G >= 256 ? G / 256 : 1;  // chunks a group spans (a chunk holds 256 elements)
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
-    if (c == 0 || G < 256 || c % (G / 256) == 0) {  // a new group starts in this chunk
+    if (c % kGroupChunks == 0) {  // a new group starts in this chunk
       gs = group_scale<SEM>(gm[c], qmax);
       r = __frcp_rn(gs.divisor);
     }
