@@ -226,9 +226,11 @@ class PagedLayer:
         if not pages:
             return
         src, dst = [], []
-        for page in pages:
+        # every new slot first: a pool that cannot hold them all raises MemoryError
+        # before any page changes (a shared pool can run out)
+        for page, new in zip(pages, self.pool.alloc_many(bits, len(pages))):
             old_bits, old = self._slots[page]
-            new = self.pool.alloc(bits)
+            new = int(new)
             ntok = min(BLOCK, self.length - page * BLOCK)
             src.append(encode(old_bits, ntok, old))
             dst.append(encode(bits, ntok, new))

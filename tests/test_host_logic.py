@@ -193,6 +193,21 @@ def test_cpu_tensors_are_refused_by_the_kernels():
         akv.pack_page(torch.randn(2, 16, 64), 4)
 
 
+def test_demotion_into_a_full_pool_changes_nothing():
+    """A PagedLayer over a shared pool with too few archive slots refuses a demotion of
+    several pages as a whole: MemoryError before any slot, view or count changes."""
+    pool = P.PagePool(2, 64, group=64, pages={16: 3, 8: 0, 4: 1}, device="cpu")
+    layer = akv.PagedLayer(2, 64, 48, group=64, pool=pool, device="cpu")
+    layer._slots = [(16, pool.alloc(16)) for _ in range(3)]  # three complete FP16 pages
+    layer.pages = [layer._views(16, off) for _, off in layer._slots]
+    layer.length = 48
+    slots, free4 = list(layer._slots), pool.free_slots(4)
+    with pytest.raises(MemoryError, match="1 free 4-bit slots, 2 requested"):
+        layer._demote_many([0, 1], 4)
+    assert layer._slots == slots and pool.free_slots(4) == free4 and layer.demotions == 0
+    assert all(k.bits == 16 for k, _ in layer.pages)
+
+
 class _Query:
     """Shape, dtype and device of a query, without a tensor (the checks run before any launch)."""
 
