@@ -137,6 +137,7 @@ class PagedLayer:
         self.recent_pages = recent_pages
         self.capacity = math.ceil(max_tokens / block)
         self.device = torch.device(device)
+        self._own_pool = pool is None  # a pool of its own may grow; a shared one is the caller's to size
         if pool is None:
             sizes = {16: self.capacity}
             if archive_bits != 16:
@@ -218,6 +219,8 @@ class PagedLayer:
             raise ValueError('lossy promotion cannot restore FP16 values')
         if page in self.protected and bits != 16:
             raise ValueError('cannot demote a protected page')
+        if bits not in (4, 8, 16):
+            raise ValueError('bits must be 4, 8, or 16')
         if bits != key.bits:
             self._demote_many([page], bits)
 
@@ -225,6 +228,12 @@ class PagedLayer:
         pages = [p for p in pages if self._slots[p][0] != bits]
         if not pages:
             return
+        if self._own_pool and self.pool.free_slots(bits) < len(pages):
+            # a precision this layer's pool has too few slots of (a manual demotion
+            # to a class other than archive_bits): grow it, which moves the arena,
+            # so every page view is rebuilt
+            self.pool.reserve(bits, len(pages))
+            self.pages = [self._views(*slot) for slot in self._slots]
         src, dst = [], []
         # every new slot first: a pool that cannot hold them all raises MemoryError
         # before any page changes (a shared pool can run out)

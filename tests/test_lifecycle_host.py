@@ -1,0 +1,148 @@
+"""Page lifecycle bookkeeping on the host, against the reference's own PagedLayer on CPU.
+
+Which pages a store demotes, when, and to what precision is host logic: the
+kernels only move the bytes.  These tests replay random append patterns
+(chunk sizes, recent windows, protected pages, archive precisions) through
+the reference's ``PagedLayer`` (packed_decode.py:108-194, installed unmodified
+in baseline/_ref, run on CPU) and through this package's ``PagedLayer`` and
+batched ``live.PagedKVStore`` with their kernel calls recorded instead of
+launched, and compare every page's precision, the demotion count, the length
+and the payload bytes.  The bytes themselves are checked against the
+reference on the GPU (tests/test_gpu_api.py, tests/test_live_route.py).
+"""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import anchorkv_b200 as akv
+from anchorkv_b200 import _lib, live
+from anchorkv_b200 import packed_decode as PD
+from anchorkv_b200 import pool as P
+
+REF_DIR = Path(__file__).resolve().parents[1] / "baseline" / "_ref"
+HEADS, DIM, GROUP = 2, 64, 64
+
+
+@pytest.fixture
+def reference(monkeypatch):
+    if not (REF_DIR / "anchorkv").exists():
+        pytest.skip("the reference is not installed in baseline/_ref")
+    monkeypatch.syspath_prepend(str(REF_DIR))
+    from anchorkv import packed_decode
+
+    return packed_decode
+
+
+@pytest.fixture
+def launches(monkeypatch):
+    """Record C-ABI calls instead of launching them; keep descriptor arrays on the host."""
+    calls = []
+    monkeypatch.setattr(_lib, "call", lambda name, *args: calls.append(name))
+    monkeypatch.setattr(_lib, "require_cuda", lambda *a, **k: None)
+    monkeypatch.setattr(_lib, "status_ptr", lambda device: 0)
+    monkeypatch.setattr(_lib, "stream_of", lambda device: 0)
+
+    def host(array, device):
+        return torch.from_numpy(np.ascontiguousarray(array, np.int64)).to(device)
+
+    monkeypatch.setattr(P, "to_device", host)
+    monkeypatch.setattr(PD, "to_device", host)
+    return calls
+
+
+def _kv(gen, tokens, batch=1):
+    shape = (batch, HEADS, tokens, DIM)
+    return torch.randn(shape, generator=gen).half(), torch.randn(shape, generator=gen).half()
+
+
+def _cases(n):
+    rng = np.random.default_rng(11)
+    for _ in range(n):
+        pages = int(rng.integers(3, 12))
+        protected = tuple(int(p) for p in rng.choice(pages, size=int(rng.integers(0, 3)), replace=False))
+        yield (int(rng.choice([4, 8, 16])), int(rng.integers(0, 4)), protected, pages,
+               [int(c) for c in rng.integers(1, 40, size=8)])
+
+
+@pytest.mark.parametrize("archive_bits,recent,protected,pages,chunks", list(_cases(12)))
+def test_paged_layer_demotes_what_the_reference_demotes(reference, launches, archive_bits, recent,
+                                                        protected, pages, chunks):
+    gen = torch.Generator().manual_seed(pages * 31 + recent)
+    max_tokens = 16 * pages
+    kw = dict(group=GROUP, archive_bits=archive_bits, protected=protected, recent_pages=recent, device="cpu")
+    ref = reference.PagedLayer(HEADS, DIM, max_tokens, **kw)
+    ours = akv.PagedLayer(HEADS, DIM, max_tokens, **kw)
+    pieces = 0  # one append launch per page a chunk writes into
+    for take in chunks:
+        take = min(take, max_tokens - ref.length)
+        if take == 0:
+            break
+        pieces += (ref.length + take - 1) // 16 - ref.length // 16 + 1
+        k, v = _kv(gen, take)
+        ref.append(k, v)
+        ours.append(k, v)
+        assert ours.length == ref.length
+        assert [kp.bits for kp, _ in ours.pages] == [kp.bits for kp, _ in ref.pages]
+        assert ours.demotions == ref.demotions
+        assert ours.payload_bytes == ref.payload_bytes
+    assert launches.count("akv_append_rows") == pieces
+    # demotions travel in batches: at most one repack launch per demoted page, none without one
+    assert (launches.count("akv_repack_pages") > 0) == (ours.demotions > 0)
+    assert launches.count("akv_repack_pages") <= ours.demotions
+    # explicit demotion to a precision the layer does not archive to (its own pool grows for it;
+    # every page view then reads the new arena) and the lifecycle errors, as the reference raises them
+    full = [p for p in range(ref.length // 16) if p not in protected and ref.pages[p][0].bits == 16]
+    if full:
+        page = full[0]
+        ref.demote(page, 8)
+        ours.demote(page, 8)
+        assert [kp.bits for kp, _ in ours.pages] == [kp.bits for kp, _ in ref.pages]
+        arena = ours.pool.arena.untyped_storage().data_ptr()
+        assert all(kp.stored.untyped_storage().data_ptr() == arena for kp, _ in ours.pages)
+        with pytest.raises(ValueError, match="lossy promotion"):
+            ours.demote(page, 16)
+        for layer in (ref, ours):
+            with pytest.raises(ValueError, match="bits must be 4, 8, or 16"):
+                layer.demote(page, 2)
+    for page in protected:
+        if page < len(ours.pages):
+            with pytest.raises(ValueError, match="protected"):
+                ours.demote(page, 4)
+
+
+@pytest.mark.parametrize("archive_bits,recent,protected,prefix,steps",
+                         [(4, 2, (), 37, 40), (8, 1, (1,), 64, 20), (4, 0, (0, 2), 5, 50), (16, 2, (), 48, 17)])
+def test_batched_store_pages_follow_the_reference_per_sequence(reference, launches, archive_bits, recent,
+                                                               protected, prefix, steps):
+    """PagedKVStore (prefill packs old pages straight to the archive precision, then one append per
+    step) leaves every sequence's pages where the reference's append-then-demote leaves them."""
+    batch, layers = 3, 2
+    gen = torch.Generator().manual_seed(prefix + steps)
+    max_tokens = prefix + steps + 3
+    store = live.PagedKVStore(layers, batch, HEADS, DIM, max_tokens, group=GROUP, archive_bits=archive_bits,
+                              recent_pages=recent, protected=protected, device="cpu")
+    refs = [[reference.PagedLayer(HEADS, DIM, max_tokens, group=GROUP, archive_bits=archive_bits,
+                                  protected=protected, recent_pages=recent, device="cpu")
+             for _ in range(batch)] for _ in range(layers)]
+    for layer in range(layers):
+        k, v = _kv(gen, prefix, batch)
+        store.prefill(layer, k, v)
+        for b in range(batch):
+            refs[layer][b].append(k[b:b + 1], v[b:b + 1])
+    for _ in range(steps):
+        for layer in range(layers):
+            k, v = _kv(gen, 1, batch)
+            store.append(layer, k, v)
+            for b in range(batch):
+                refs[layer][b].append(k[b:b + 1], v[b:b + 1])
+    for layer in range(layers):
+        expected = np.array([[kp.bits for kp, _ in r.pages] for r in refs[layer]])
+        np.testing.assert_array_equal(store.bits(layer), expected)
+        assert store.lengths[layer] == refs[layer][0].length
+    assert store.demotions == sum(r.demotions for rs in refs for r in rs)
+    assert store.payload_bytes == sum(r.payload_bytes for rs in refs for r in rs)
+    assert launches.count("akv_pack_pages") == layers
+    assert launches.count("akv_append_rows") == layers * steps
