@@ -55,3 +55,8 @@ class CachePlan:
         if self.used_bytes == 0:
             return math.inf if self.full_cache_bytes else 1.0
         return self.full_cache_bytes / self.used_bytes
+
+    @property
+    def budget_utilization(self) -> float:
+        """Planned bytes over the budget (0 without a budget), policy.py:163-165."""
+        return self.used_bytes / self.budget_bytes if self.budget_bytes else 0.0

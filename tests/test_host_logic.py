@@ -7,12 +7,9 @@ import pytest
 import torch
 
 import anchorkv_b200 as akv
-from anchorkv_b200 import backend as B
 from anchorkv_b200 import pool as P
 from anchorkv_b200.policy import CacheMode
-from oracle import codec as OC
-
-_KERNEL_QUANTIZE = B.quantize_tensor  # FP16/EVICTED modes need no kernel
+from host_codec import use_oracle_codec
 
 
 def test_descriptor_round_trip():
@@ -111,33 +108,9 @@ def test_parser_matches_reference_behaviour():
     assert p2.feed("<global>")[0].mode == akv.AttentionMode.GLOBAL  # bad tag was consumed
 
 
-def _oracle_quantize(tensor, mode, *, group_size=64):
-    """CPU stand-in for the kernel, used only to exercise host logic here."""
-    mode = CacheMode(getattr(mode, "value", mode))
-    if mode in (CacheMode.FP16, CacheMode.EVICTED):
-        return _KERNEL_QUANTIZE(tensor, mode, group_size=group_size)
-    bits = 8 if mode is CacheMode.INT8 else 4
-    payload, scales = OC.quantize_tensor(tensor.detach().float().numpy(), bits, group_size)
-    return B.PackedTensor(mode, tuple(tensor.shape), tensor.dtype, torch.from_numpy(payload),
-                          torch.from_numpy(scales), group_size, tensor.numel())
-
-
-def _oracle_dequantize(self, *, dtype=None, device=None):
-    if self.mode is CacheMode.EVICTED or self.payload is None:
-        raise RuntimeError("evicted tensors cannot be materialized")
-    out_dtype = self.original_dtype if dtype is None else dtype
-    if self.mode is CacheMode.FP16:
-        return self.payload.to(out_dtype).reshape(self.shape)
-    bits = 8 if self.mode is CacheMode.INT8 else 4
-    vals = OC.dequantize_tensor(self.payload.numpy(), self.scales.numpy(), bits, self.group_size,
-                                self.original_numel)
-    return torch.from_numpy(vals).reshape(self.shape).to(out_dtype)
-
-
 @pytest.fixture
 def cpu_cache(monkeypatch):
-    monkeypatch.setattr(B, "quantize_tensor", _oracle_quantize)
-    monkeypatch.setattr(B.PackedTensor, "dequantize", _oracle_dequantize)
+    use_oracle_codec(monkeypatch)
     torch.manual_seed(11)
     cache = akv.DeclarativeKVCache(block_size=4, group_size=16)
     for sid, start, count, role in [(0, 0, 4, akv.SegmentRole.SINK), (1, 4, 6, akv.SegmentRole.CONTEXT),
