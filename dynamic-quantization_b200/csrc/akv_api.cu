@@ -39,7 +39,8 @@ extern "C" int akv_status_alloc(void **host_ptr, void **dev_ptr) {
 }
 
 extern "C" int akv_status_free(void *host_ptr) {
-  return host_ptr && cudaFreeHost(host_ptr) == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+  if (!host_ptr) return AKV_ERR_INVALID;
+  return cudaFreeHost(host_ptr) == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
 }
 
 extern "C" int64_t akv_record_bytes(int head_dim, int group, int mode) {

@@ -1498,10 +1498,14 @@ extern "C" int akv_ipc_open(const void *handle, void **ptr) {
 }
 
 extern "C" int akv_ipc_close(void *ptr) {
-  return ptr && cudaIpcCloseMemHandle(ptr) == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+  if (!ptr) return AKV_ERR_INVALID;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
 }
 
-extern "C" int akv_ipc_free(void *ptr) { return ptr && cudaFree(ptr) == cudaSuccess ? AKV_OK : AKV_ERR_CUDA; }
+extern "C" int akv_ipc_free(void *ptr) {
+  if (!ptr) return AKV_ERR_INVALID;
+  return cudaFree(ptr) == cudaSuccess ? AKV_OK : AKV_ERR_CUDA;
+}
 
 extern "C" int akv_merge_states(const float *states, int32_t n, int32_t batch, int32_t q_heads,
                                 int32_t head_dim, void *out, int64_t out_batch_stride,
