@@ -159,3 +159,37 @@ def test_every_entry_point_checks_its_arguments_before_a_launch():
     assert lib.akv_ipc_open(None, ctypes.byref(out)) == inval
     assert lib.akv_ipc_close(None) == inval and lib.akv_ipc_free(None) == inval
     assert lib.akv_status_alloc(None, None) == inval and lib.akv_status_free(None) == inval
+
+
+C_CALLER = r"""
+#include "anchorkv_b200.h"
+#include <stdio.h>
+int main(void) {
+  /* host-only calls: no GPU needed */
+  long long int4_record = (long long)akv_record_bytes(128, 2048, AKV_MODE_INT4);
+  int empty = akv_quantize(0, AKV_DTYPE_F16, 0, 16, 8, AKV_SEM_TENSOR, 0, 0, 0);
+  printf("%d %lld %d %lld\n", akv_abi_version(), int4_record, empty, (long long)akv_static_scratch_bytes());
+  return 0;
+}
+"""
+
+
+@pytest.mark.parametrize("compiler,flags", [("gcc", ["-std=c99", "-pedantic", "-Wall", "-Wextra", "-Werror"]),
+                                            ("g++", ["-std=c++17", "-Wall", "-Wextra", "-Werror", "-x", "c++"])])
+def test_header_serves_c_and_cxx_callers(tmp_path, compiler, flags):
+    """A C or C++ program includes the header, links the library and calls it,
+    with no Python in between (the binding a C or C++ host would add)."""
+    import shutil
+    import subprocess
+
+    if shutil.which(compiler) is None:
+        pytest.skip(f"{compiler} is not installed")
+    src, exe = tmp_path / "caller.c", tmp_path / "caller"
+    src.write_text(C_CALLER)
+    libdir = _lib.LIB_PATH.parent
+    subprocess.run([compiler, *flags, "-I", str(ROOT / "include"), str(src), "-L", str(libdir), "-lanchorkv_b200",
+                    f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True, capture_output=True, text=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
+    lib = _lib.load()
+    assert out == [str(lib.akv_abi_version()), str(P.record_bytes(128, 2048, 4)), str(_lib.ERR_INVALID),
+                   str(lib.akv_static_scratch_bytes())]
