@@ -129,3 +129,23 @@ def test_stack_legacy_cache(ref):
 
     for source in [tuple(kv), Cache, (), ((kv[0][0],),), (kv[0], (kv[1][0][..., :4, :], kv[1][1]))]:
         _both(lambda: RB.stack_legacy_cache(source), lambda: akv.stack_legacy_cache(source))
+
+
+def test_packed_attention_argument_errors(ref, monkeypatch):
+    """The checks triton_decode.py:86-94 makes before any launch, on empty CPU layers of
+    both implementations (the kernels are never reached)."""
+    monkeypatch.syspath_prepend(str(REF_DIR))
+    from anchorkv import triton_decode
+
+    _, RP, _ = ref
+    ref_layer = RP.PagedLayer(2, 64, 64, device="cpu")
+    our_layer = akv.PagedLayer(2, 64, 64, device="cpu")
+    g = torch.Generator().manual_seed(7)
+    queries = [torch.randn(2, 4, 1, 64, generator=g).half(),   # batch 2
+               torch.randn(1, 4, 3, 64, generator=g).half(),   # three query tokens
+               torch.randn(1, 4, 1, 32, generator=g).half(),   # head_dim mismatch
+               torch.randn(1, 4, 1, 64, generator=g).half(),   # a CPU query (and an empty cache)
+               torch.randn(1, 4, 1, 64, generator=g)]          # fp32
+    for q in queries:
+        _both(lambda: triton_decode.packed_attention(q, ref_layer, 0.125),
+              lambda: akv.packed_attention(q, our_layer, 0.125))
