@@ -1248,17 +1248,18 @@ def run_kernels(args):
         out = torch.empty_like(x)
         q_bytes = 2 * n + n // 2 + 2 * (n // 64)
         if want("quantize_flat"):
-            timed("quantize_flat_kernel<half,4,tensor>", q_bytes,
+            timed("quantize_vec_kernel<half,4,tensor>", q_bytes,
                   lambda: _lib.call("akv_quantize", x.data_ptr(), _lib.DTYPE_F16, n, 64, 4, _lib.SEM_TENSOR,
                                     payload.data_ptr(), scales.data_ptr(), sptr),
-                  "256 Mi fp16 elements to INT4, group 64 (quantize_tensor)")
+                  "256 Mi fp16 elements to INT4, group 64 (quantize_tensor; whole power-of-two groups of "
+                  "8-256 take the vector kernel)")
         if want("dequantize_flat"):
             _lib.call("akv_quantize", x.data_ptr(), _lib.DTYPE_F16, n, 64, 4, _lib.SEM_TENSOR, payload.data_ptr(),
                       scales.data_ptr(), sptr)
-            timed("dequantize_flat_kernel<half,4>", q_bytes,
+            timed("dequantize_vec_kernel<half,4>", q_bytes,
                   lambda: _lib.call("akv_dequantize", payload.data_ptr(), scales.data_ptr(), n, 64, 4,
                                     out.data_ptr(), _lib.DTYPE_F16, sptr),
-                  "256 Mi INT4 elements to fp16, group 64 (PackedTensor.dequantize)")
+                  "256 Mi INT4 elements to fp16, group 64 (PackedTensor.dequantize; the vector kernel)")
         del x, payload, scales, out
     if want("unpack_pages") or want("repack_pages"):
         wl = WORKLOADS["batched_small"]
