@@ -31,7 +31,7 @@ from .backend import (
     quantize_tensor,
     stack_legacy_cache,
 )
-from .decode import decode_partial_states, merge_states, packed_attention
+from .decode import decode_partial_states, merge_states, packed_attention, query_head_to_kv_head
 from .packed_decode import PagedLayer, QuantizedPage, dense_attention, kl_divergence, pack_page, tensor_bytes
 from .policy import CacheMode, CachePlan, PlannedSegment
 from .pool import PagedBatch, PagePool, pack_dense
@@ -48,5 +48,5 @@ __all__ = [
     "SegmentRecord", "SegmentRole", "decode_partial_states", "dense_attention", "kl_divergence",
     "merge_states", "pack_page", "packed_attention", "quantize_tensor", "stack_legacy_cache",
     "take_device_status", "tensor_bytes", "pack_dense", "shard_range", "gather_states",
-    "sharded_packed_attention",
+    "sharded_packed_attention", "query_head_to_kv_head",
 ]

@@ -63,6 +63,22 @@ def _as_table(layer):
     return layer
 
 
+def query_head_to_kv_head(query_head: int, *, num_query_heads: int, num_kv_heads: int) -> int:
+    """The KV head a query head reads under grouped-query attention
+    (heads.py:112-126): ``query_head // (num_query_heads // num_kv_heads)``.
+
+    The decode kernel serves every query head of one KV head from the same
+    pages with this map (a warp's slot holds that KV head's query heads,
+    consecutive in the query); the checks and errors are the reference's."""
+    if num_query_heads <= 0 or num_kv_heads <= 0:
+        raise ValueError("head counts must be positive")
+    if num_query_heads % num_kv_heads != 0:
+        raise ValueError("num_query_heads must be divisible by num_kv_heads")
+    if not 0 <= query_head < num_query_heads:
+        raise ValueError("query_head is out of range")
+    return query_head // (num_query_heads // num_kv_heads)
+
+
 def _check_query(query, layer, splits, *, empty_ok: bool) -> int:
     """The argument checks of triton_decode.py:86-94, in its order and with its
     messages, for a page table of ``layer``; returns the batch.

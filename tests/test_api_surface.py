@@ -26,6 +26,7 @@ REPLACED = {
     "packed_decode": ["PagedLayer", "pack_page", "QuantizedPage", "dense_attention", "kl_divergence",
                       "tensor_bytes"],
     "triton_decode": ["packed_attention"],
+    "heads": ["query_head_to_kv_head"],
 }
 
 

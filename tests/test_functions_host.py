@@ -149,3 +149,15 @@ def test_packed_attention_argument_errors(ref, monkeypatch):
     for q in queries:
         _both(lambda: triton_decode.packed_attention(q, ref_layer, 0.125),
               lambda: akv.packed_attention(q, our_layer, 0.125))
+
+
+def test_gqa_head_map(ref, monkeypatch):
+    """query_head_to_kv_head (heads.py:112-126), the map the decode kernel serves query heads by."""
+    monkeypatch.syspath_prepend(str(REF_DIR))
+    from anchorkv import heads
+
+    for hq in (0, 1, 4, 8, 12, 16, 32, -8):
+        for hkv in (0, 1, 2, 3, 4, 8, -1):
+            for q in (-1, 0, 1, 3, 7, 15, 31, 32):
+                _both(lambda: heads.query_head_to_kv_head(q, num_query_heads=hq, num_kv_heads=hkv),
+                      lambda: akv.query_head_to_kv_head(q, num_query_heads=hq, num_kv_heads=hkv))
