@@ -89,19 +89,29 @@ class PeerExchange:
         own = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
         _lib.call("akv_ipc_alloc", nbytes, ctypes.byref(own), handle)
-        handles = [None] * self.world
-        dist.all_gather_object(handles, handle.raw, group=group)
         self._own = own.value
         self._mapped = []
         ptrs = []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                ptrs.append(self._own)
-                continue
-            peer = ctypes.c_void_p()
-            _lib.call("akv_ipc_open", ctypes.create_string_buffer(h, 64), ctypes.byref(peer))
-            self._mapped.append(peer.value)
-            ptrs.append(peer.value)
+        try:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                peer = ctypes.c_void_p()
+                _lib.call("akv_ipc_open", ctypes.create_string_buffer(h, 64), ctypes.byref(peer))
+                self._mapped.append(peer.value)
+                ptrs.append(peer.value)
+        except BaseException:
+            # nothing has been launched on these buffers: unmap what was mapped and
+            # free this rank's buffer before the error reaches the caller (the other
+            # ranks learn of it from their process group's timeout)
+            for ptr in self._mapped:
+                _lib.load().akv_ipc_close(ctypes.c_void_p(ptr))
+            _lib.load().akv_ipc_free(ctypes.c_void_p(self._own))
+            self._mapped, self._own = [], None
+            raise
         self._peers = (ctypes.c_void_p * self.world)(*ptrs)
         self.epoch = 0
         dist.barrier(group=group)

@@ -265,3 +265,48 @@ def test_reported_device_errors_raise_on_the_next_call(monkeypatch):
     with pytest.raises(akv.KernelError, match="misaligned.*bounded wait"):
         _lib.raise_pending("fake-device")
     assert _lib.describe_status(8).startswith("unknown")
+
+
+def test_peer_exchange_setup_failure_releases_its_buffers(monkeypatch):
+    """A rank that cannot map a peer's exchange buffer unmaps what it mapped and frees
+    its own buffer before raising (library and process group replaced by recorders)."""
+    from anchorkv_b200 import _lib
+    from anchorkv_b200 import sharded as S
+
+    released = []
+
+    class FakeLib:
+        def akv_exchange_bytes(self, world, batch, q_heads, dim):
+            return 4096
+
+        def akv_ipc_close(self, ptr):
+            released.append(("close", ptr.value))
+            return 0
+
+        def akv_ipc_free(self, ptr):
+            released.append(("free", ptr.value))
+            return 0
+
+    opened = []
+
+    def call(name, *args):
+        if name == "akv_ipc_alloc":
+            args[1]._obj.value = 0x1000  # this rank's buffer
+        elif name == "akv_ipc_open":
+            if len(opened) == 1:
+                raise akv.KernelError("akv_ipc_open: CUDA launch error")
+            opened.append(0x2000)
+            args[1]._obj.value = 0x2000
+        else:
+            raise AssertionError(name)
+
+    monkeypatch.setattr(_lib, "load", lambda *a: FakeLib())
+    monkeypatch.setattr(_lib, "call", call)
+    monkeypatch.setattr(S.dist, "get_world_size", lambda group=None: 3)
+    monkeypatch.setattr(S.dist, "get_rank", lambda group=None: 0)
+    monkeypatch.setattr(S.dist, "all_gather_object", lambda out, obj, group=None: out.__setitem__(
+        slice(None), [obj, b"\1" * 64, b"\2" * 64]))
+    monkeypatch.setattr(S.dist, "barrier", lambda group=None: pytest.fail("no barrier after a failed setup"))
+    with pytest.raises(akv.KernelError, match="akv_ipc_open"):
+        S.PeerExchange(1, 32, 128)
+    assert released == [("close", 0x2000), ("free", 0x1000)]
