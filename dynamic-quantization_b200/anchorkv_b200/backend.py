@@ -597,6 +597,7 @@ class DeclarativeKVCache:
 
     def _add_pages(self, seg: _Segment, key: torch.Tensor, value: torch.Tensor) -> None:
         heads = seg.lead[-1]
+        status, stream = _lib.status_ptr(key.device), _lib.stream_of(key.device)  # raises before any change
         if self._pool is None:
             self._pool = P.PagePool(heads, seg.dim, group=self.group_size, device=key.device)
             self._table_geometry = (seg.lead, seg.dim, key.device)
@@ -620,8 +621,7 @@ class DeclarativeKVCache:
         d = P.to_device(desc.reshape(-1), dev)
         _lib.call("akv_pack_pages", k.data_ptr(), v.data_ptr(), heads * nblk * P.BLOCK * seg.dim,
                   nblk * P.BLOCK * seg.dim, nblk, rows * nblk, d.data_ptr(), self._pool.arena.data_ptr(),
-                  self._pool.nbytes, heads, seg.dim, self.group_size, _lib.SEM_TENSOR, _lib.status_ptr(dev),
-                  _lib.stream_of(dev))
+                  self._pool.nbytes, heads, seg.dim, self.group_size, _lib.SEM_TENSOR, status, stream)
         seg.columns = self._grow_columns(nblk)
         self._descriptors[:, seg.columns] = desc
 
@@ -636,6 +636,8 @@ class DeclarativeKVCache:
         return list(range(first, first + n))
 
     def _requantize_pages(self, seg: _Segment, mode: CacheMode) -> None:
+        dev = self._pool.device
+        status, stream = _lib.status_ptr(dev), _lib.stream_of(dev)  # raises before any change
         old = self._descriptors[:, seg.columns]
         offsets = old >> 8
         if mode is CacheMode.EVICTED:
@@ -645,12 +647,10 @@ class DeclarativeKVCache:
             self._pool.reserve(bits, old.size)
             fresh = self._pool.alloc_many(bits, old.size).reshape(old.shape)
             new = P.encode_array(np.full(old.shape, P.BITS_TO_MODE[bits]), ((old >> 2) & 15) + 1, fresh)
-            dev = self._pool.device
             src, dst = P.to_device(old.reshape(-1), dev), P.to_device(new.reshape(-1), dev)
             heads = self._table_geometry[0][-1]
             _lib.call("akv_repack_pages", src.data_ptr(), dst.data_ptr(), old.size, self._pool.arena.data_ptr(),
-                      self._pool.nbytes, heads, seg.dim, self.group_size, _lib.SEM_TENSOR, _lib.status_ptr(dev),
-                      _lib.stream_of(dev))
+                      self._pool.nbytes, heads, seg.dim, self.group_size, _lib.SEM_TENSOR, status, stream)
             self._descriptors[:, seg.columns] = new
         # stream order: anything later written into the freed slots follows the repack
         self._pool.free_many(_BITS[seg.mode], offsets)

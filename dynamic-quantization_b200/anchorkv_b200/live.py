@@ -88,6 +88,7 @@ class PagedKVStore:
         if tokens > self.capacity * P.BLOCK:
             raise ValueError("cache geometry or capacity exceeded")
         _lib.require_cuda(key, "key")
+        status, stream = _lib.status_ptr(self.device), _lib.stream_of(self.device)  # raises before any change
         n = -(-tokens // P.BLOCK)
         eligible = tokens // P.BLOCK - self.recent_pages  # complete pages older than the recent window
         bits = np.full(n, 16)
@@ -110,7 +111,7 @@ class PagedKVStore:
         d = P.to_device(desc.reshape(-1), self.device)
         _lib.call("akv_pack_pages", k.data_ptr(), v.data_ptr(), heads * n * P.BLOCK * dim, n * P.BLOCK * dim, n,
                   batch * n, d.data_ptr(), self.pool.arena.data_ptr(), self.pool.nbytes, heads, dim, self.group,
-                  _lib.SEM_PAGE, _lib.status_ptr(self.device), _lib.stream_of(self.device))
+                  _lib.SEM_PAGE, status, stream)
         self.tables[layer, :, :n].copy_(d.view(batch, n))
         self.demotions += batch * int((bits != 16).sum())  # the reference appends, then demotes, these pages
         self._desc[layer, :, :n] = desc
@@ -153,9 +154,11 @@ class PagedKVStore:
     def _archive(self, layer: int) -> None:
         last = self.lengths[layer] // P.BLOCK - self.recent_pages - 1
         pages = [p for p in range(self._archived[layer] + 1, last + 1) if p not in self.protected]
-        self._archived[layer] = max(self._archived[layer], last)
         if self.archive_bits == 16 or not pages:
+            self._archived[layer] = max(self._archived[layer], last)
             return
+        status, stream = _lib.status_ptr(self.device), _lib.stream_of(self.device)  # raises before any change
+        self._archived[layer] = max(self._archived[layer], last)
         src = self._desc[layer][:, pages]  # [batch, n]
         self.pool.reserve(self.archive_bits, src.size)
         offs = self.pool.alloc_many(self.archive_bits, src.size)
@@ -163,8 +166,7 @@ class PagedKVStore:
                              offs.reshape(src.shape))
         s_dev, d_dev = P.to_device(src.reshape(-1), self.device), P.to_device(dst.reshape(-1), self.device)
         _lib.call("akv_repack_pages", s_dev.data_ptr(), d_dev.data_ptr(), src.size, self.pool.arena.data_ptr(),
-                  self.pool.nbytes, self.heads, self.dim, self.group, _lib.SEM_PAGE, _lib.status_ptr(self.device),
-                  _lib.stream_of(self.device))
+                  self.pool.nbytes, self.heads, self.dim, self.group, _lib.SEM_PAGE, status, stream)
         self.tables[layer].index_copy_(1, P.to_device(pages, self.device), d_dev.view(src.shape))
         self._desc[layer][:, pages] = dst
         self.pool.free_many(16, src >> 8)  # stream order: later writes to these slots follow the repack

@@ -184,6 +184,8 @@ class PagedLayer:
         _lib.require_cuda(key, "key")
         key, value = as_fp16_rows(key), as_fp16_rows(value)
         dev = self.device
+        # an error an earlier kernel reported is raised here, before any page changes
+        status, stream = _lib.status_ptr(dev), _lib.stream_of(dev)
         offset = 0
         while offset < key.shape[-2]:
             page, position = divmod(self.length, self.block)
@@ -200,7 +202,7 @@ class PagedLayer:
             _lib.call("akv_append_rows", k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2), 1,
                       take, position, self.table.data_ptr(), self.capacity, page,
                       None if fresh is None else fresh.data_ptr(), self.pool.arena.data_ptr(), self.pool.nbytes,
-                      self.heads, self.dim, _lib.status_ptr(dev), _lib.stream_of(dev))
+                      self.heads, self.dim, status, stream)
             self.length += take
             offset += take
             self._archive_old_pages()
@@ -228,15 +230,16 @@ class PagedLayer:
         pages = [p for p in pages if self._slots[p][0] != bits]
         if not pages:
             return
+        dev = self.device
+        status, stream = _lib.status_ptr(dev), _lib.stream_of(dev)  # an earlier kernel's error, before any change
         if self._own_pool and self.pool.free_slots(bits) < len(pages):
             # a precision this layer's pool has too few slots of (a manual demotion
             # to a class other than archive_bits): grow it, which moves the arena,
             # so every page view is rebuilt
             self.pool.reserve(bits, len(pages))
             self.pages = [self._views(*slot) for slot in self._slots]
+        self.pool.check_free(bits, len(pages))  # a shared pool can run out: raises before any page changes
         src, dst = [], []
-        # every new slot first: a pool that cannot hold them all raises MemoryError
-        # before any page changes (a shared pool can run out)
         for page, new in zip(pages, self.pool.alloc_many(bits, len(pages))):
             old_bits, old = self._slots[page]
             new = int(new)
@@ -244,11 +247,10 @@ class PagedLayer:
             src.append(encode(old_bits, ntok, old))
             dst.append(encode(bits, ntok, new))
             self._slots[page] = (bits, new)
-        dev = self.device
         src_t, dst_t = to_device(src, dev), to_device(dst, dev)  # pinned, non-blocking: no host stall
         _lib.call("akv_repack_pages", src_t.data_ptr(), dst_t.data_ptr(), len(pages),
                   self.pool.arena.data_ptr(), self.pool.nbytes, self.heads, self.dim, self.group,
-                  _lib.SEM_PAGE, _lib.status_ptr(dev), _lib.stream_of(dev))
+                  _lib.SEM_PAGE, status, stream)
         for page, d in zip(pages, src):
             old_bits = {1: 4, 2: 8, 3: 16}[d & 3]
             self.pool.free(old_bits, d >> 8)  # stream order: later writes follow the repack

@@ -160,9 +160,13 @@ class PagePool:
             raise MemoryError(f"page pool has no free {bits}-bit page slots")
         return int(self._free[bits].pop())
 
-    def alloc_many(self, bits: int, n: int) -> np.ndarray:
+    def check_free(self, bits: int, n: int) -> None:
+        """Raise MemoryError unless ``n`` slots of ``bits`` are free (nothing changes)."""
         if n > len(self._free[bits]):
             raise MemoryError(f"page pool has {len(self._free[bits])} free {bits}-bit slots, {n} requested")
+
+    def alloc_many(self, bits: int, n: int) -> np.ndarray:
+        self.check_free(bits, n)
         if n == 0:
             return np.zeros(0, np.int64)
         out = np.array(self._free[bits][-n:][::-1], dtype=np.int64)
@@ -286,17 +290,20 @@ def pack_dense(pool: PagePool, key: torch.Tensor, value: torch.Tensor, block_bit
     ntok = np.clip(lengths[:, None] - j * BLOCK, 1, BLOCK)
     offsets = np.zeros((batch, nblk), np.int64)
     codes = np.zeros((batch, nblk), np.int64)
+    for b_ in BITS_TO_MODE:  # every class checked before any slot is taken
+        pool.check_free(b_, int((bits == b_).sum()))
+    dev = pool.device
+    status, stream = _lib.status_ptr(dev), _lib.stream_of(dev)  # an earlier kernel's error, before any change
     for b_, mode in BITS_TO_MODE.items():
         where = bits == b_
         offsets[where] = pool.alloc_many(b_, int(where.sum()))
         codes[where] = mode
     desc = encode_array(codes, ntok, offsets)
-    dev = pool.device
     dst = torch.from_numpy(desc.reshape(-1)).to(dev)
     sem = _lib.SEM_TENSOR if semantics == "tensor" else _lib.SEM_PAGE
     _lib.call("akv_pack_pages", key.data_ptr(), value.data_ptr(), heads * padded * dim, padded * dim,
               nblk, batch * nblk, dst.data_ptr(), pool.arena.data_ptr(), pool.nbytes, heads, dim,
-              pool.group, sem, _lib.status_ptr(dev), _lib.stream_of(dev))
+              pool.group, sem, status, stream)
     out = PagedBatch(pool, batch, nblk)
     if visible is not None:
         desc = np.where(np.asarray(visible, bool).reshape(batch, nblk), desc, 0)

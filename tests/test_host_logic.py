@@ -166,9 +166,13 @@ def test_cpu_tensors_are_refused_by_the_kernels():
         akv.pack_page(torch.randn(2, 16, 64), 4)
 
 
-def test_demotion_into_a_full_pool_changes_nothing():
+def test_demotion_into_a_full_pool_changes_nothing(monkeypatch):
     """A PagedLayer over a shared pool with too few archive slots refuses a demotion of
     several pages as a whole: MemoryError before any slot, view or count changes."""
+    from anchorkv_b200 import _lib
+
+    monkeypatch.setattr(_lib, "status_ptr", lambda device: 0)  # host stand-ins: no kernel runs here
+    monkeypatch.setattr(_lib, "stream_of", lambda device: 0)
     pool = P.PagePool(2, 64, group=64, pages={16: 3, 8: 0, 4: 1}, device="cpu")
     layer = akv.PagedLayer(2, 64, 48, group=64, pool=pool, device="cpu")
     layer._slots = [(16, pool.alloc(16)) for _ in range(3)]  # three complete FP16 pages

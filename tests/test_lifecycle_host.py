@@ -146,3 +146,73 @@ def test_batched_store_pages_follow_the_reference_per_sequence(reference, launch
     assert store.payload_bytes == sum(r.payload_bytes for rs in refs for r in rs)
     assert launches.count("akv_pack_pages") == layers
     assert launches.count("akv_append_rows") == layers * steps
+
+
+@pytest.fixture
+def pending(launches, monkeypatch):
+    """After ``pending.set()``, the status word reports an earlier kernel's error, as
+    ``_lib.status_ptr`` does when a finished kernel left a bit."""
+
+    class Pending:
+        on = False
+
+        def set(self):
+            self.on = True
+
+    flag = Pending()
+
+    def status_ptr(device):
+        if flag.on:
+            raise akv.KernelError("an earlier kernel on cuda:0 reported: a page descriptor outside the arena")
+        return 0
+
+    monkeypatch.setattr(_lib, "status_ptr", status_ptr)
+    return flag
+
+
+def _pool_state(pool):
+    return {b: pool.free_slots(b) for b in (16, 8, 4)}, pool.nbytes
+
+
+def test_a_reported_device_error_leaves_every_store_unchanged(pending):
+    """The error an earlier kernel reported is raised before a store changes anything:
+    no slot is taken, no page or descriptor moves, no count advances."""
+    gen = torch.Generator().manual_seed(2)
+    layer = akv.PagedLayer(HEADS, DIM, 160, group=GROUP, archive_bits=4, recent_pages=1, device="cpu")
+    layer.append(*_kv(gen, 48))  # whole pages: the next append takes a fresh slot
+    before = (layer.length, list(layer._slots), [k.bits for k, _ in layer.pages], layer.demotions,
+              _pool_state(layer.pool), layer.table.clone())
+    pending.set()
+    assert [k.bits for k, _ in layer.pages] == [4, 4, 16]  # pages 0-1 archived, page 2 recent
+    for step in (lambda: layer.append(*_kv(gen, 30)), lambda: layer.demote(2, 8),
+                 lambda: layer._demote_many([2], 4)):
+        with pytest.raises(akv.KernelError, match="reported"):
+            step()
+        after = (layer.length, list(layer._slots), [k.bits for k, _ in layer.pages], layer.demotions,
+                 _pool_state(layer.pool), layer.table.clone())
+        assert after[:5] == before[:5] and torch.equal(after[5], before[5])
+
+    pending.on = False
+    store = live.PagedKVStore(2, 3, HEADS, DIM, 96, group=GROUP, archive_bits=4, recent_pages=1, device="cpu")
+    store.prefill(0, *_kv(gen, 50, batch=3))
+    snap = (list(store.lengths), store._desc.copy(), list(store._archived), store.demotions, _pool_state(store.pool))
+    pending.set()
+    for step in (lambda: store.append(0, *_kv(gen, 1, batch=3)), lambda: store.prefill(1, *_kv(gen, 20, batch=3))):
+        with pytest.raises(akv.KernelError, match="reported"):
+            step()
+        assert (store.lengths, store._archived, store.demotions, _pool_state(store.pool)) == \
+            (snap[0], snap[2], snap[3], snap[4])
+        np.testing.assert_array_equal(store._desc, snap[1])
+    store.lengths[0] += 16  # a page became eligible for the archive: the archive step raises first too
+    with pytest.raises(akv.KernelError, match="reported"):
+        store._archive(0)
+    assert store._archived == snap[2] and _pool_state(store.pool) == snap[4]
+
+    pool = P.PagePool(HEADS, DIM, group=GROUP, pages={16: 4, 8: 4, 4: 4}, device="cpu")
+    with pytest.raises(akv.KernelError, match="reported"):
+        P.pack_dense(pool, *_kv(gen, 32, batch=2), [[16, 8], [4, 0]], semantics="page")
+    assert _pool_state(pool) == ({16: 4, 8: 4, 4: 4}, pool.nbytes)
+    pending.on = False
+    with pytest.raises(MemoryError, match="2 free 16-bit slots, 3 requested"):
+        P.pack_dense(P.PagePool(HEADS, DIM, group=GROUP, pages={16: 2, 8: 4, 4: 0}, device="cpu"),
+                     *_kv(gen, 32, batch=2), [[16, 8], [16, 16]], semantics="page")
