@@ -758,7 +758,7 @@ def long_context_leg(args, device, rank: int, world: int, local: int, wl: dict =
 
     import anchorkv_b200 as akv
     from anchorkv_b200 import _lib
-    from anchorkv_b200.sharded import PeerExchange, sharded_packed_attention
+    from anchorkv_b200.sharded import PeerExchange, next_epoch, sharded_packed_attention
 
     wl = LONG if wl is None else wl
     Hq, Hkv, D = wl["q_heads"], wl["kv_heads"], wl["dim"]
@@ -787,7 +787,7 @@ def long_context_leg(args, device, rank: int, world: int, local: int, wl: dict =
             assert lib.akv_merge(ws.data_ptr(), 1, Hq, D, out.data_ptr(), out.stride(0), out.stride(1), None,
                                  status.data_ptr(), sptr) == 0
             return
-        exchange.epoch += 1  # merge, exchange over NVLink and merge again in one kernel
+        exchange.epoch = next_epoch(exchange.epoch)  # merge, exchange over NVLink and merge again in one kernel
         assert lib.akv_merge_exchange(ws.data_ptr(), 1, Hq, D, exchange._peers, exchange.rank, world,
                                       exchange.epoch, out.data_ptr(), out.stride(0), out.stride(1),
                                       status.data_ptr(), sptr) == 0

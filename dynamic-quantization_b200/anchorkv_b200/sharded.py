@@ -65,6 +65,21 @@ def sharded_packed_attention(query, local_store, scale, *, splits=0, group=None,
     return merge(gather_states(state, group))
 
 
+EPOCH_MAX = 0xFFFFFFFF  # the exchange kernel's epoch is a 32-bit word; 0 marks a buffer never written
+
+
+def next_epoch(epoch: int) -> int:
+    """The epoch of the exchange call after one with ``epoch`` (0 before the first call).
+
+    The kernel needs each call's epoch to be nonzero, to alternate in parity
+    (the parity picks the buffer half) and to differ from the epoch two calls
+    before (the stale words in that half carry it).  Counting up does all
+    three until 32 bits run out; after ``0xFFFFFFFF`` (odd) the count goes on
+    at 2 (even), whose half holds words tagged ``0xFFFFFFFE``.  Every rank
+    applies the same rule, so their epochs stay equal."""
+    return epoch + 1 if epoch < EPOCH_MAX else 2
+
+
 class PeerExchange:
     """Cross-GPU LSE merge over peer memory for sequences split over the ranks
     of ``group`` (one process per GPU of one node, at most 8).
@@ -147,7 +162,7 @@ class PeerExchange:
                   None if seq_blocks is None else seq_blocks.data_ptr(), max_blocks, query.data_ptr(),
                   query.stride(0), query.stride(1), self.batch, self.q_heads, local_store.heads, self.dim,
                   local_store.group, float(scale), splits, ws.data_ptr(), ws.numel(), status, stream)
-        self.epoch += 1
+        self.epoch = next_epoch(self.epoch)
         _lib.call("akv_merge_exchange", ws.data_ptr(), self.batch, self.q_heads, self.dim, self._peers,
                   self.rank, self.world, self.epoch, out.data_ptr(), out.stride(0), out.stride(1), status,
                   stream)

@@ -224,7 +224,9 @@ int64_t akv_exchange_bytes(int32_t world, int32_t batch, int32_t q_heads, int32_
  *   peer_buffers[r]: rank r's exchange buffer as mapped in this process
  *     (akv_ipc_alloc / akv_ipc_open), zeroed before the first call;
  *   epoch: 1 for the first call on these buffers, +1 for each following call,
- *     the same on every rank.  Every rank must make the same calls.
+ *     the same on every rank; after 0xFFFFFFFF it goes on at 2 (any nonzero
+ *     value works that alternates in parity and differs from the epoch two
+ *     calls before).  Every rank must make the same calls.
  * Calls of even and odd epochs use separate halves of the buffers, so a rank
  * may run one call ahead of a slower peer: it writes epoch e + 1's states into
  * the other half while the peer still reads epoch e's, and it cannot reach

@@ -27,11 +27,17 @@ def value(src, epoch, word):
     return (src * 1000 + epoch) * 10 + word
 
 
-def run(world, epochs, halves, seed):
+def run(world, epochs, halves, seed, tags=None):
     """Returns None if every call of every rank completed with the right values,
-    else a string naming the first violation (a wrong value or a stuck wait)."""
+    else a string naming the first violation (a wrong value or a stuck wait).
+
+    ``tags[e]`` is the epoch word call ``e`` (1-based) passes to the kernel
+    (default: ``e``); the kernel compares tags only, so the model records each
+    word's call beside its tag to see whether a matching tag ever names the
+    wrong call."""
     rng = random.Random(seed)
-    buf = [[[[(0, 0)] * WORDS for _ in range(world)] for _ in range(halves)] for _ in range(world)]
+    tags = list(range(epochs + 1)) if tags is None else tags
+    buf = [[[[(0, 0, 0)] * WORDS for _ in range(world)] for _ in range(halves)] for _ in range(world)]
     call = [0] * world           # last completed call per rank
     phase = ["idle"] * world     # idle -> stored (publishing) -> done
     pending = [None] * world     # word stores of the current call not yet landed
@@ -58,7 +64,7 @@ def run(world, epochs, halves, seed):
             return f"deadlock: ranks {stuck} wait for words that never carry their epoch"
         kind, r = rng.choice(actions)
         e = call[r] + 1
-        half = e % halves
+        half = tags[e] % halves
         if kind == "start":  # the decode of call e ran; the exchange kernel begins storing
             pending[r] = [(p, w) for p in range(world) for w in range(WORDS)]
             rng.shuffle(pending[r])
@@ -66,17 +72,17 @@ def run(world, epochs, halves, seed):
             phase[r] = "stored"
         elif kind == "land":  # one word store reaches rank p's buffer
             p, w = pending[r].pop()
-            buf[p][half][r][w] = (e, value(r, e, w))
+            buf[p][half][r][w] = (e, tags[e], value(r, e, w))
         elif kind == "poll":  # the waiting CTA reads one word of its own buffer
             idx = rng.choice([i for i, v in enumerate(seen[r]) if v is None])
             src, w = divmod(idx, WORDS)
-            tag, v = buf[r][half][src][w]
-            if tag == e:
-                if v != value(src, e, w):
-                    return f"rank {r} call {e} read {v} from rank {src}, expected {value(src, e, w)}"
+            writer, tag, v = buf[r][half][src][w]
+            if tag == tags[e]:  # what the kernel checks
+                if writer != e or v != value(src, e, w):
+                    return f"rank {r} call {e} read {v} from rank {src}'s call {writer}, expected {value(src, e, w)}"
                 seen[r][idx] = v
-            elif tag > e:
-                return f"deadlock: rank {r} call {e} finds rank {src}'s word already at call {tag}"
+            elif writer > e:
+                return f"deadlock: rank {r} call {e} finds rank {src}'s word already at call {writer}"
         elif kind == "finish":  # the grid completes; the next decode may start
             call[r] = e
             phase[r] = "idle"
@@ -92,3 +98,32 @@ def test_one_half_lets_a_fast_rank_overwrite_an_unread_word():
     failures = [run(2, epochs=7, halves=1, seed=s) for s in range(400)]
     assert any(f is not None for f in failures)
     assert all(f is None or f.startswith("deadlock") for f in failures)
+
+
+def _host_tags(first, epochs):
+    """Epoch words of calls 1..epochs as PeerExchange issues them, the first being ``first``."""
+    from anchorkv_b200.sharded import next_epoch
+
+    tags = [0, first]
+    while len(tags) <= epochs:
+        tags.append(next_epoch(tags[-1]))
+    return tags
+
+
+def test_epochs_that_run_out_of_32_bits_keep_the_halves_apart():
+    """Across the wrap of the 32-bit epoch (0xFFFFFFFF, then 2, 3, ...) calls still
+    alternate halves and never take a word of another call for their own."""
+    tags = _host_tags(0xFFFFFFFC, 9)
+    assert tags[1:] == [0xFFFFFFFC, 0xFFFFFFFD, 0xFFFFFFFE, 0xFFFFFFFF, 2, 3, 4, 5, 6]
+    assert all(t != 0 for t in tags[1:])
+    for world in (2, 3, 4):
+        for seed in range(300):
+            assert run(world, epochs=9, halves=2, seed=seed, tags=tags) is None, (world, seed)
+
+
+def test_a_wrap_that_repeats_a_parity_is_caught():
+    """Wrapping 0xFFFFFFFF to 1 would put two consecutive calls in one half, the race
+    the halves exist to remove; the model finds it."""
+    tags = [0, 0xFFFFFFFE, 0xFFFFFFFF, 1, 2, 3, 4, 5]
+    failures = [run(2, epochs=7, halves=2, seed=s, tags=tags) for s in range(400)]
+    assert any(f is not None for f in failures)
