@@ -37,11 +37,24 @@ def _workspace_bytes(device: torch.device, *geometry) -> int:
     return nbytes
 
 
+_MAX_WORKSPACES = 64
+
+
 def _workspace(device: torch.device, nbytes: int, stream: int | None = None) -> torch.Tensor:
+    """The decode workspace of (device, stream), grown on demand.
+
+    Workspaces of at most ``_MAX_WORKSPACES`` streams are kept; the oldest goes
+    first (a caller that makes a stream per request would otherwise hold one
+    per stream forever).  Dropping one is safe: it was allocated on its own
+    stream and used only there, so the allocator reuses its memory in that
+    stream's order."""
     key = (device.index, torch.cuda.current_stream(device).cuda_stream if stream is None else stream)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _workspaces.pop(key, None)
+        while len(_workspaces) >= _MAX_WORKSPACES:
+            _workspaces.pop(next(iter(_workspaces)))
         _workspaces[key] = ws
     return ws
 

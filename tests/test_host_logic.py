@@ -314,3 +314,23 @@ def test_peer_exchange_setup_failure_releases_its_buffers(monkeypatch):
     with pytest.raises(akv.KernelError, match="akv_ipc_open"):
         S.PeerExchange(1, 32, 128)
     assert released == [("close", 0x2000), ("free", 0x1000)]
+
+
+def test_decode_workspaces_are_kept_for_a_bounded_number_of_streams():
+    from anchorkv_b200 import decode as D
+
+    cpu = torch.device("cpu")
+    saved = dict(D._workspaces)
+    D._workspaces.clear()
+    try:
+        first = D._workspace(cpu, 100, stream=1)
+        assert D._workspace(cpu, 100, stream=1) is first  # reused on its stream
+        for s in range(2, 2 + 3 * D._MAX_WORKSPACES):
+            D._workspace(cpu, 100, stream=s)
+        assert len(D._workspaces) == D._MAX_WORKSPACES
+        assert (None, 1) not in D._workspaces and (None, 1 + 3 * D._MAX_WORKSPACES) in D._workspaces
+        grown = D._workspace(cpu, 1 << 20, stream=1 + 3 * D._MAX_WORKSPACES)  # a larger request replaces it
+        assert grown.numel() == 1 << 20 and len(D._workspaces) == D._MAX_WORKSPACES
+    finally:
+        D._workspaces.clear()
+        D._workspaces.update(saved)
