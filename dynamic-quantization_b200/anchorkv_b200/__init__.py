@@ -10,8 +10,11 @@ kernels behind a C ABI (``include/anchorkv_b200.h``):
 * :class:`PagedLayer` (batch one) and :class:`PagedBatch` over a shared
   :class:`PagePool` arena, :class:`DeclarativeKVCache` for segment-level
   visibility and eviction;
-* :func:`packed_attention`, the paged split-K decode with an LSE merge, and
-  :func:`decode_partial_states` / :func:`merge_states` for merging across GPUs.
+* :func:`packed_attention`, the paged split-K decode with an LSE merge
+  (query heads served by :func:`query_head_to_kv_head`'s map), and
+  :func:`decode_partial_states` / :func:`merge_states` for merging across GPUs;
+  ``anchorkv_b200.sharded`` adds the NVLink exchange of one long sequence's
+  shards and ``anchorkv_b200.live`` batched Hugging Face decode.
 """
 
 from .backend import (
