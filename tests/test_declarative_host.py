@@ -166,3 +166,27 @@ def test_random_programs_match_the_reference(reference, seed):
         program.step()
     if program.layers:  # the legacy cache view of 5-D segments
         program.both(lambda c, M, Pm: c.materialize_visible().to_legacy_cache())
+
+
+PARSER_PIECES = ["<", ">", "<<", ">>", "focus", "FOCUS", "Focus", "/focus", "local", "/local", "global", "anchor",
+                 "archive", " ", "  ", "segments", "magic_chunks", "SEGMENTS", "=", " = ", '"', "'", "1", "2", "17",
+                 ",", ", ", "-", "x", "\n", "<focus segments=\"3\">", "</focus>", "<archive segments='4,5'>",
+                 "<anchor segments=\"2, 2\">", "< global >", "<local/>", "<focusx segments=\"1\">", "<>",
+                 "<local>", "< LOCAL >", "</local>", "<focus segments=\"1,,2\">", "<archive segments=\"-3\">",
+                 "<anchor magic_chunks='0'>"]
+
+
+@pytest.mark.parametrize("seed", range(30))
+def test_parser_fuzz_matches_the_reference(reference, seed):
+    """Random streams of tag fragments, fed in random chunks, give the same directives,
+    errors and parser state after every chunk as the reference's parser."""
+    RB, _ = reference
+    rng = np.random.default_rng(1000 + seed)
+    ours, ref = akv.DeclarativeAttentionParser(), RB.DeclarativeAttentionParser()
+    for _ in range(60):
+        chunk = "".join(str(rng.choice(PARSER_PIECES)) for _ in range(int(rng.integers(1, 6))))
+        a = _outcome(lambda: ref.feed(chunk))
+        b = _outcome(lambda: ours.feed(chunk))
+        assert a == b, (chunk, a, b)
+        assert (ref.state.mode.value, ref.state.focus_segment_ids) == \
+            (ours.state.mode.value, ours.state.focus_segment_ids), chunk
