@@ -10,13 +10,10 @@ are allowed).
 """
 
 import inspect
-from pathlib import Path
-
 import pytest
 
 import anchorkv_b200 as akv
 
-REF_DIR = Path(__file__).resolve().parents[1] / "baseline" / "_ref"
 REPLACED = {
     "backend": ["quantize_tensor", "PackedTensor", "DeclarativeKVCache", "SegmentRole", "AttentionMode",
                 "DirectiveKind", "CacheDirective", "DeclarativeAttentionParser", "DeclarativeState",
@@ -31,16 +28,10 @@ REPLACED = {
 
 
 @pytest.fixture(scope="module")
-def reference():
-    if not (REF_DIR / "anchorkv").exists():
-        pytest.skip("the reference is not installed in baseline/_ref")
-    mp = pytest.MonkeyPatch()
-    mp.syspath_prepend(str(REF_DIR))
+def reference(reference_install):
     import importlib
 
-    mods = {name: importlib.import_module(f"anchorkv.{name}") for name in REPLACED}
-    yield mods
-    mp.undo()
+    return {name: importlib.import_module(f"anchorkv.{name}") for name in REPLACED}
 
 
 def _default(value):

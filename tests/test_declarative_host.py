@@ -14,8 +14,6 @@ CPU tensors take the flat-segment path, whose codec calls run the oracle here
 compared with the reference on the GPU (tests/test_gpu_declarative.py).
 """
 
-from pathlib import Path
-
 import numpy as np
 import pytest
 import torch
@@ -23,16 +21,12 @@ import torch
 import anchorkv_b200 as akv
 from host_codec import use_oracle_codec
 
-REF_DIR = Path(__file__).resolve().parents[1] / "baseline" / "_ref"
 MODES = ("fp16", "int8", "int4", "evicted")
 ROLES = ("sink", "scaffold", "context", "response")
 
 
 @pytest.fixture
-def reference(monkeypatch):
-    if not (REF_DIR / "anchorkv").exists():
-        pytest.skip("the reference is not installed in baseline/_ref")
-    monkeypatch.syspath_prepend(str(REF_DIR))
+def reference(reference_install, monkeypatch):
     from anchorkv import backend, policy
 
     use_oracle_codec(monkeypatch)

@@ -8,26 +8,18 @@ must be equal bit for bit, errors equal in type name and message.  INT8/INT4
 values are compared with the reference on the GPU (tests/test_gpu_codec.py).
 """
 
-from pathlib import Path
-
 import pytest
 import torch
 
 import anchorkv_b200 as akv
 
-REF_DIR = Path(__file__).resolve().parents[1] / "baseline" / "_ref"
 
 
 @pytest.fixture(scope="module")
-def ref():
-    if not (REF_DIR / "anchorkv").exists():
-        pytest.skip("the reference is not installed in baseline/_ref")
-    mp = pytest.MonkeyPatch()
-    mp.syspath_prepend(str(REF_DIR))
+def ref(reference_install):
     from anchorkv import backend, packed_decode, policy
 
-    yield backend, packed_decode, policy
-    mp.undo()
+    return backend, packed_decode, policy
 
 
 def _outcome(fn):
@@ -131,10 +123,9 @@ def test_stack_legacy_cache(ref):
         _both(lambda: RB.stack_legacy_cache(source), lambda: akv.stack_legacy_cache(source))
 
 
-def test_packed_attention_argument_errors(ref, monkeypatch):
+def test_packed_attention_argument_errors(ref):
     """The checks triton_decode.py:86-94 makes before any launch, on empty CPU layers of
     both implementations (the kernels are never reached)."""
-    monkeypatch.syspath_prepend(str(REF_DIR))
     from anchorkv import triton_decode
 
     _, RP, _ = ref
@@ -151,9 +142,8 @@ def test_packed_attention_argument_errors(ref, monkeypatch):
               lambda: akv.packed_attention(q, our_layer, 0.125))
 
 
-def test_gqa_head_map(ref, monkeypatch):
+def test_gqa_head_map(ref):
     """query_head_to_kv_head (heads.py:112-126), the map the decode kernel serves query heads by."""
-    monkeypatch.syspath_prepend(str(REF_DIR))
     from anchorkv import heads
 
     for hq in (0, 1, 4, 8, 12, 16, 32, -8):

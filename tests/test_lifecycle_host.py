@@ -11,8 +11,6 @@ and the payload bytes.  The bytes themselves are checked against the
 reference on the GPU (tests/test_gpu_api.py, tests/test_live_route.py).
 """
 
-from pathlib import Path
-
 import numpy as np
 import pytest
 import torch
@@ -22,15 +20,11 @@ from anchorkv_b200 import _lib, live
 from anchorkv_b200 import packed_decode as PD
 from anchorkv_b200 import pool as P
 
-REF_DIR = Path(__file__).resolve().parents[1] / "baseline" / "_ref"
 HEADS, DIM, GROUP = 2, 64, 64
 
 
 @pytest.fixture
-def reference(monkeypatch):
-    if not (REF_DIR / "anchorkv").exists():
-        pytest.skip("the reference is not installed in baseline/_ref")
-    monkeypatch.syspath_prepend(str(REF_DIR))
+def reference(reference_install):
     from anchorkv import packed_decode
 
     return packed_decode

@@ -16,7 +16,6 @@ over the same stores, which holds for any weights."""
 
 import gc
 import weakref
-from pathlib import Path
 
 import pytest
 import torch
@@ -24,7 +23,6 @@ import torch
 import anchorkv_b200 as akv
 from anchorkv_b200 import live
 
-REF_DIR = Path(__file__).resolve().parents[1] / "baseline" / "_ref"
 
 
 def _qwen3(head_dim, heads, kv_heads, layers, device, dtype, seed=0):
@@ -38,13 +36,10 @@ def _qwen3(head_dim, heads, kv_heads, layers, device, dtype, seed=0):
 
 
 @pytest.fixture
-def reference(monkeypatch):
+def reference(reference_install, monkeypatch):
     """The reference's colab_experiment / benchmark_suite modules with this
     package substituted for its block store and kernels (a one-line import
     change for a user of the reference)."""
-    if not (REF_DIR / "anchorkv").exists():
-        pytest.skip("the reference is not installed in baseline/_ref")
-    monkeypatch.syspath_prepend(str(REF_DIR))
     from anchorkv import benchmark_suite, colab_experiment, triton_decode
 
     monkeypatch.setattr(colab_experiment, "PagedLayer", akv.PagedLayer)
